@@ -1,0 +1,558 @@
+"""Benchmark of the spTiles hot path on B200: matmul TFLOP/s and vector_add HBM GB/s.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl ours|reference]
+
+Under torchrun (N > 1) each rank drives one GPU; the work is sharded with the
+library's partitioner (matmul by M-row blocks, vector_add by element range:
+strong scaling, total work fixed) and the reported time is the maximum over
+ranks of the device-timed region.  Rank 0 prints one JSON line.
+
+Workloads (synthetic inputs of the configured shapes and distributions):
+  matmul_f16     C[8192,8192] f32 = A f16 @ B f16, A,B ~ N(0, 0.1), seed 3   (default headline)
+  matmul_bf16    C[32768,4096] bf16 = A bf16 @ B bf16 + bias, N(0, 0.05), seed 4
+  matmul_fp32    C[1024,1024] = A @ B, f32 via 3xTF32, N(0, 1), seed 2
+  vector_add_2d  C = A + B, f32 4096 x 4096, U[-1, 1), seed 1
+  vector_add_1d  C = A + B, f32 2^20, U[-1, 1), seed 0
+The default run also measures vector_add_2d and reports it under "vecadd".
+
+A step is one call of the hot path over one batch.  Device time: CUDA events
+on the stream the kernels run on, bracketed by a barrier and a synchronize.
+Between timed steps either the inputs exceed the 126 MB L2 (matmul), or the
+step rotates through enough buffer sets to exceed it (vector_add).
+
+--impl reference times the reference's algorithm on the host cores instead:
+the CPU restatement of its shader arithmetic (the reference itself cannot be
+built or run here), on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "matmul TFLOP/s & vecadd HBM GB/s at 1/2/4/8 B200, % of roofline"
+L2_BYTES = 126 * 1024 * 1024
+
+WORKLOADS = {
+    "matmul_f16": dict(kind="matmul", m=8192, n=8192, k=8192, dtype="f16", out="f32", bias=False, std=0.1, seed=3),
+    "matmul_bf16": dict(kind="matmul", m=32768, n=4096, k=4096, dtype="bf16", out="bf16", bias=True, std=0.05,
+                        seed=4),
+    "matmul_fp32": dict(kind="matmul", m=1024, n=1024, k=1024, dtype="f32", out="f32", bias=False, std=1.0, seed=2),
+    "vector_add_2d": dict(kind="vector_add", shape=(4096, 4096), seed=1),
+    "vector_add_1d": dict(kind="vector_add", shape=(2 ** 20,), seed=0),
+}
+
+
+def parse_args():
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=100)
+    p.add_argument("--warmup", type=int, default=10)
+    p.add_argument("--workload", default="matmul_f16", choices=sorted(WORKLOADS))
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--no-secondary", action="store_true", help="skip the vector_add measurement of the default run")
+    p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    return rank, world, local
+
+
+def measured_peaks():
+    f = ROOT / "MEASURED_PEAKS.json"
+    if f.exists():
+        d = json.loads(f.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained"), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+def profile_traffic(key: str):
+    """DRAM bytes per launch from the committed ncu summary, if one exists."""
+    f = ROOT / "profiles" / "traffic_per_launch.txt"
+    if not f.exists():
+        return None
+    for line in f.read_text().splitlines():
+        parts = line.split()
+        if len(parts) >= 2 and parts[0] == key:
+            try:
+                return float(parts[1])
+            except ValueError:
+                return None
+    return None
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """Samples SM clock and clock-event reasons through NVML while running."""
+
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+               0x80: "hw_power_brake_slowdown", 0x2: "applications_clocks_setting"}
+
+    def __init__(self, device_index: int, period_s: float = 0.002):
+        self.samples, self.reasons, self.max_mhz = [], 0, None
+        self._stop = threading.Event()
+        self._thread = None
+        self.error = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception as e:  # pragma: no cover - depends on the box
+            self._nv = None
+            self.error = str(e)
+        self.period = period_s
+
+    def _run(self):
+        nv = self._nv
+        get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+                self.reasons |= int(get_reasons(self._h))
+            except Exception as e:  # pragma: no cover
+                self.error = str(e)
+                return
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self._nv is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread:
+            self._thread.join()
+
+    def summary(self):
+        if self._nv is None or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": len(self.samples),
+                    "note": self.error or "no samples"}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": [v for k, v in self.REASONS.items() if self.reasons & k], "samples": len(self.samples),
+                "source": "NVML during the timed region"}
+
+
+# ------------------------------------------------------------------ inputs
+def torch_dtype(name):
+    import torch
+    return {"f16": torch.float16, "bf16": torch.bfloat16, "f32": torch.float32}[name]
+
+
+def make_matmul_inputs(wl, rows, device, seed_offset=0):
+    """This rank's A rows, B and bias, generated on the device."""
+    import torch
+    g = torch.Generator(device=device).manual_seed(wl["seed"] * 1000 + seed_offset)
+    dt = torch_dtype(wl["dtype"])
+    a = (torch.randn((rows, wl["k"]), generator=g, device=device) * wl["std"]).to(dt)
+    gb = torch.Generator(device=device).manual_seed(wl["seed"] * 1000 + 999)
+    b = (torch.randn((wl["k"], wl["n"]), generator=gb, device=device) * wl["std"]).to(dt)
+    bias = None
+    if wl["bias"]:
+        bias = (torch.rand(wl["n"], generator=gb, device=device) * 2 - 1).to(dt)
+    return a, b, bias
+
+
+def flops_of(wl, rows):
+    f = 2.0 * rows * wl["n"] * wl["k"]
+    if wl["bias"]:
+        f += rows * wl["n"]
+    return f
+
+
+# ------------------------------------------------------------------ our arm
+def time_steps(fn, steps, warmup, stream, dist_on):
+    """Per-step device time (ms) of `fn` over `steps` calls after `warmup` calls."""
+    import torch
+    import torch.distributed as dist
+    for _ in range(warmup):
+        fn(-1)
+    torch.cuda.synchronize()
+    if dist_on:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for i in range(steps):
+        fn(i)
+    end.record(stream)
+    torch.cuda.synchronize()
+    if dist_on:
+        dist.barrier()
+    return start.elapsed_time(end)
+
+
+def max_over_ranks(x, dist_on):
+    if not dist_on:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(x, dist_on):
+    if not dist_on:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+def run_matmul(wl, args, rank, world, local, dist_on, peaks):
+    import torch
+    import sptiles_b200 as st
+    from sptiles_b200.partition import matmul_row_shard
+
+    dev = torch.device("cuda", local)
+    r0, r1 = matmul_row_shard(wl["m"], world, rank)
+    rows = r1 - r0
+    a, b, bias = make_matmul_inputs(wl, rows, dev, seed_offset=rank)
+    out_dt = torch_dtype(wl["out"])
+    c = torch.empty((rows, wl["n"]), dtype=out_dt, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step(_i):
+        if rows:
+            st.matmul(a, b, bias, out=c)
+
+    launches0 = st.kernel_launches()
+    with ClockSampler(local) as clk:
+        ms = time_steps(step, args.steps, args.warmup, stream, dist_on)
+    launches = st.kernel_launches() - launches0 - args.warmup * (1 if rows else 0) * per_call_launches(wl)
+    ms_max = max_over_ranks(ms, dist_on)
+    total_flops = sum_over_ranks(flops_of(wl, rows), dist_on)
+    value = total_flops * args.steps / (ms_max / 1e3) / 1e12
+    per_launch_ms = ms / args.steps
+    achieved = flops_of(wl, rows) / (per_launch_ms / 1e3) / 1e12 if rows else 0.0
+    peak = peaks["bf16_tflops"]
+    if wl["dtype"] == "f32":
+        peak = peaks["bf16_tflops"] / 2.0 / 3.0  # tf32 runs at half the 16-bit rate, 3 passes
+    key = f"matmul_{wl['dtype']}_{wl['m']}x{wl['n']}x{wl['k']}"
+    traffic = profile_traffic(key)
+    plan = st.matmul_plan({"f16": 1, "bf16": 2, "f32": 0}[wl["dtype"]], rows or 1, wl["n"], wl["k"])
+    roof = {"bound": "tensor", "achieved": round(achieved, 2), "peak": round(peak, 1), "unit": "TFLOP/s",
+            "frac": round(achieved / peak, 4),
+            "peak_note": ("of measured dense bf16 cuBLAS burst peak (fp16 has the same dense rate)"
+                          if wl["dtype"] != "f32" else "of measured bf16 peak / 2 (tf32 rate) / 3 (3xTF32 passes)")
+            if peaks["source"] == "measured" else "of fallback peak",
+            "traffic": traffic, "kernel": "gemm_tc_kernel", "ms_per_launch": round(per_launch_ms, 4)}
+    out = dict(value=value, ms_per_step=ms_max / args.steps, roofline=roof, gpu_launches=int(launches),
+               clocks=clk.summary(), plan=plan, rows=rows)
+    if not args.no_e2e:
+        out["e2e"] = e2e_matmul(wl, args, a, b, bias, out_dt, rows, dist_on)
+    return out
+
+
+def per_call_launches(wl):
+    return 3 if wl["dtype"] == "f32" else 1
+
+
+def e2e_matmul(wl, args, a, b, bias, out_dt, rows, dist_on):
+    """Same metric through the public API on pinned host buffers (copies in the timed region)."""
+    import torch
+    import sptiles_b200 as st
+    ha = a.cpu().pin_memory()
+    hb = b.cpu().pin_memory()
+    hbias = bias.cpu().pin_memory() if bias is not None else None
+    hc = torch.empty((rows, wl["n"]), dtype=out_dt).pin_memory()
+    steps = max(1, min(args.steps, 10))
+    for _ in range(2):
+        if rows:
+            st.matmul(ha, hb, hbias, out=hc)
+    if dist_on:
+        import torch.distributed as dist
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        if rows:
+            st.matmul(ha, hb, hbias, out=hc)  # returns once C is back in host memory
+    dt = time.perf_counter() - t0
+    dt = max_over_ranks(dt, dist_on)
+    total_flops = sum_over_ranks(flops_of(wl, rows), dist_on)
+    h2d = ha.numel() * ha.element_size() + hb.numel() * hb.element_size() + \
+        (hbias.numel() * hbias.element_size() if hbias is not None else 0)
+    d2h = hc.numel() * hc.element_size()
+    return {"value": round(total_flops * steps / dt / 1e12, 3), "unit": "TFLOP/s", "h2d_bytes_per_step": int(h2d),
+            "d2h_bytes_per_step": int(d2h), "steps": steps,
+            "how": "sptiles_b200.matmul on pinned host tensors (st_matmul_host): H2D, kernel, D2H per step, "
+                   "host wall clock"}
+
+
+def run_vector_add(wl, args, rank, world, local, dist_on, peaks):
+    import torch
+    import sptiles_b200 as st
+    from sptiles_b200.partition import vector_add_shard
+
+    dev = torch.device("cuda", local)
+    total = math.prod(wl["shape"])
+    e0, e1 = vector_add_shard(total, world, rank)
+    n = e1 - e0
+    bytes_per_step = 12 * n
+    # enough buffer sets that one round trip exceeds twice the L2
+    sets = max(1, math.ceil(2 * L2_BYTES / max(1, bytes_per_step)))
+    sets = min(sets, 64)
+    g = torch.Generator(device=dev).manual_seed(wl["seed"] * 1000 + rank)
+    shape_local = (n,) if len(wl["shape"]) == 1 else None
+    bufs = []
+    for _ in range(sets):
+        a = torch.rand(n, generator=g, device=dev) * 2 - 1
+        b = torch.rand(n, generator=g, device=dev) * 2 - 1
+        c = torch.empty(n, device=dev)
+        if len(wl["shape"]) == 2 and world == 1:
+            a, b, c = (x.view(wl["shape"]) for x in (a, b, c))
+        bufs.append((a, b, c))
+    stream = torch.cuda.current_stream(dev)
+
+    def step(i):
+        a, b, c = bufs[i % sets]
+        st.vector_add(a, b, out=c)
+
+    launches0 = st.kernel_launches()
+    with ClockSampler(local) as clk:
+        ms = time_steps(step, args.steps, args.warmup, stream, dist_on)
+    launches = st.kernel_launches() - launches0 - args.warmup
+    ms_max = max_over_ranks(ms, dist_on)
+    total_bytes = sum_over_ranks(bytes_per_step, dist_on)
+    value = total_bytes * args.steps / (ms_max / 1e3) / 1e9
+    achieved = bytes_per_step / (ms / args.steps / 1e3) / 1e9
+    key = "vector_add_" + "x".join(str(s) for s in wl["shape"])
+    roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+            "frac": round(achieved / peaks["hbm_gbs"], 4),
+            "peak_note": "of measured copy bandwidth" if peaks["source"] == "measured" else "of fallback",
+            "traffic": profile_traffic(key), "kernel": "vadd_vec4_kernel",
+            "ms_per_launch": round(ms / args.steps, 5)}
+    out = dict(value=value, ms_per_step=ms_max / args.steps, roofline=roof, gpu_launches=int(launches),
+               clocks=clk.summary(), sets=sets, elements=n)
+    if not args.no_e2e:
+        a, b, c = bufs[0]
+        ha, hb = a.cpu().pin_memory(), b.cpu().pin_memory()
+        hc = torch.empty_like(ha).pin_memory()
+        steps = max(1, min(args.steps, 20))
+        st.vector_add(ha, hb, out=hc)
+        if dist_on:
+            import torch.distributed as dist
+            dist.barrier()
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            st.vector_add(ha, hb, out=hc)
+        dt = max_over_ranks(time.perf_counter() - t0, dist_on)
+        out["e2e"] = {"value": round(total_bytes * steps / dt / 1e9, 2), "unit": "GB/s",
+                      "h2d_bytes_per_step": 8 * n, "d2h_bytes_per_step": 4 * n, "steps": steps,
+                      "how": "sptiles_b200.vector_add on pinned host tensors (st_vector_add_host), host wall clock"}
+    return out
+
+
+# ------------------------------------------------------------------ CPU side
+class CpuMatmul:
+    """The oracle (CPU restatement of the shader arithmetic) on row samples of a workload."""
+
+    def __init__(self, wl, threads):
+        import numpy as np
+        import oracle
+        self.wl, self.threads, self.oracle = wl, threads, oracle
+        rng = np.random.default_rng(wl["seed"])
+        k, n = wl["k"], wl["n"]
+        self.bf = wl["dtype"] == "bf16"
+
+        def gen(shape):
+            x = (rng.standard_normal(shape, dtype=np.float32) * np.float32(wl["std"]))
+            if wl["dtype"] == "f16":
+                return x.astype(np.float16)
+            if self.bf:
+                return oracle.f32_to_bf16_bits(x).reshape(shape)
+            return x
+
+        self.gen = gen
+        self.b = gen((k, n))
+        self.bias = None
+        if wl["bias"]:
+            u = rng.uniform(-1, 1, n).astype(np.float32)
+            self.bias = oracle.f32_to_bf16_bits(u) if self.bf else u
+        self.a = gen((min(wl["m"], 256), k))
+        self.out = {"f32": oracle.F32, "f16": oracle.F16, "bf16": oracle.BF16}[wl["out"]]
+
+    def rows_for(self, budget_s):
+        probe = max(self.threads, 8)
+        t = self.run(probe)
+        return int(max(1, min(self.wl["m"], budget_s / max(t / probe, 1e-9))))
+
+    def run(self, rows):
+        import numpy as np
+        while self.a.shape[0] < rows:
+            self.a = np.concatenate([self.a, self.gen((min(rows, self.wl["m"]) - self.a.shape[0], self.wl["k"]))])
+        t, _ = self.oracle.time_matmul_rows(self.a[:rows], self.b, self.bias, bf16=self.bf, out_dtype=self.out,
+                                            rows=rows, threads=self.threads)
+        return t
+
+
+class CpuVectorAdd:
+    def __init__(self, wl):
+        import numpy as np
+        import oracle
+        self.oracle = oracle
+        n = math.prod(wl["shape"])
+        rng = np.random.default_rng(wl["seed"])
+        self.a = rng.uniform(-1, 1, n).astype(np.float32)
+        self.b = rng.uniform(-1, 1, n).astype(np.float32)
+        self.c = np.empty_like(self.a)
+        self.n = n
+
+    def reps_for(self, budget_s):
+        return max(1, int(budget_s / max(self.oracle.time_vector_add(self.a, self.b, self.c, 1), 1e-6)))
+
+    def run(self, reps):
+        return self.oracle.time_vector_add(self.a, self.b, self.c, reps) * reps
+
+
+def cpu_baseline(wl, budget_s=10.0):
+    threads = os.cpu_count() or 1
+    if wl["kind"] == "matmul":
+        cm = CpuMatmul(wl, threads)
+        rows = cm.rows_for(budget_s)
+        t = cm.run(rows)
+        v = flops_of(wl, rows) / t / 1e12
+        return {"value": round(v, 5), "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                "sample": f"first {rows} of {wl['m']} rows of C ({rows}x{wl['n']}x{wl['k']}), {t:.1f} s, "
+                          "oracle restatement of the shader arithmetic, -O3 -ffp-contract=off, "
+                          f"{threads} threads; throughput extrapolates linearly in rows"}
+    cv = CpuVectorAdd(wl)
+    reps = cv.reps_for(budget_s)
+    t = cv.run(reps)
+    return {"value": round(12 * cv.n * reps / t / 1e9, 3), "unit": "GB/s", "cores": 1, "kind": "port",
+            "sample": f"{reps} full passes over {cv.n} elements, {t:.1f} s, one thread"}
+
+
+def run_reference(args, rank, world):
+    """The reference arm: its arithmetic on the host cores, rank 0 only."""
+    if rank != 0:
+        return 0
+    wl = WORKLOADS[args.workload]
+    threads = os.cpu_count() or 1
+    per_step_budget = max(0.3, min(4.0, 150.0 / max(1, args.steps + args.warmup)))
+    vals = []
+    if wl["kind"] == "matmul":
+        cm = CpuMatmul(wl, threads)
+        rows = cm.rows_for(per_step_budget)
+        for i in range(args.warmup + args.steps):
+            t = cm.run(rows)
+            if i >= args.warmup:
+                vals.append(flops_of(wl, rows) / t / 1e12)
+        detail = (f"each step: first {rows} of {wl['m']} rows of C ({rows}x{wl['n']}x{wl['k']}) on {threads} "
+                  "threads; CPU restatement of the shader arithmetic (-O3 -ffp-contract=off)")
+        unit, cores = "TFLOP/s", threads
+    else:
+        cv = CpuVectorAdd(wl)
+        reps = cv.reps_for(per_step_budget)
+        for i in range(args.warmup + args.steps):
+            t = cv.run(reps)
+            if i >= args.warmup:
+                vals.append(12 * cv.n * reps / t / 1e9)
+        detail = f"each step: {reps} passes over {cv.n} elements, one thread"
+        unit, cores = "GB/s", 1
+    value = statistics.median(vals)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": unit, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": wl.get("dtype", "f32"), "data": "synthetic",
+        "config": config_of(args.workload, wl, args.gpus),
+        "cpu_baseline": {"value": value, "unit": unit, "cores": cores, "kind": "port", "sample": detail},
+        "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference's SPIR-V runs through Vulkan, which is unavailable on this box, and its "
+                "translator cannot be built here; this arm runs the CPU restatement of its shader arithmetic",
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def config_of(name, wl, n_gpus):
+    if wl["kind"] == "matmul":
+        return {"workload": name, "M": wl["m"], "N": wl["n"], "K": wl["k"], "in_dtype": wl["dtype"],
+                "out_dtype": wl["out"], "bias": wl["bias"], "parallelism": f"M-row shards x{n_gpus}",
+                "l2": "inputs exceed L2 (A+B > 126 MB)" if wl["m"] * wl["k"] * 2 > L2_BYTES else
+                      "inputs fit in L2"}
+    total = math.prod(wl["shape"])
+    return {"workload": name, "shape": list(wl["shape"]), "dtype": "f32", "parallelism": f"element shards x{n_gpus}",
+            "l2": "steps rotate through buffer sets totalling > 2x L2"}
+
+
+def main():
+    args = parse_args()
+    rank, world, local = dist_env()
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+    import torch
+    torch.cuda.set_device(local)
+    dist_on = world > 1
+    if dist_on:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                device_id=torch.device("cuda", local))
+    peaks = measured_peaks()
+    wl = WORKLOADS[args.workload]
+    try:
+        if wl["kind"] == "matmul":
+            res = run_matmul(wl, args, rank, world, local, dist_on, peaks)
+        else:
+            res = run_vector_add(wl, args, rank, world, local, dist_on, peaks)
+        secondary = None
+        if args.workload == "matmul_f16" and not args.no_secondary:
+            vw = WORKLOADS["vector_add_2d"]
+            sub = run_vector_add(vw, args, rank, world, local, dist_on, peaks)
+            secondary = {"workload": "vector_add_2d", "value": round(sub["value"], 1), "unit": "GB/s",
+                         "ms_per_step": round(sub["ms_per_step"], 5), "roofline": sub["roofline"],
+                         "e2e": sub.get("e2e"), "gpu_launches": sub["gpu_launches"], "clocks": sub["clocks"],
+                         "config": config_of("vector_add_2d", vw, world)}
+        cpu = None
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+            cpu = cpu_baseline(wl)
+        if rank == 0:
+            line = {
+                "metric": METRIC, "value": round(res["value"], 3),
+                "unit": "TFLOP/s" if wl["kind"] == "matmul" else "GB/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": round(res["ms_per_step"], 5), "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": wl.get("dtype", "f32"),
+                "data": "synthetic (seeded; shapes and distributions of the configuration)",
+                "config": config_of(args.workload, wl, world), "roofline": res["roofline"],
+                "cpu_baseline": cpu, "e2e": res.get("e2e"), "gpu_launches": res["gpu_launches"],
+                "clocks": res["clocks"],
+            }
+            if wl["kind"] == "matmul":
+                line["config"]["tile"] = f"{res['plan']['block_m']}x{res['plan']['block_n']}x{res['plan']['block_k']}"
+                line["config"]["ctas"] = res["plan"]["ctas"]
+            if secondary:
+                line["vecadd"] = secondary
+            print(json.dumps(line), flush=True)
+    finally:
+        if dist_on:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

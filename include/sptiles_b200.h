@@ -1,0 +1,188 @@
+/*
+ * sptiles_b200.h -- C ABI of the B200 (sm_100a) backend for the two cuda_tile
+ * workloads that spTiles compiles: the elementwise tile add (vector_add, 1D
+ * and 2D) and the tiled mmaf matmul.
+ *
+ * Plain C types only: pointers, sizes, int status codes.  No C++ exceptions
+ * and no framework types cross this boundary.  Every function returns an
+ * ST_* status; st_last_error() gives the message of the calling thread's
+ * last failure.  One host thread drives one context.
+ *
+ * What each group replaces in the reference (paths within the spTiles tree):
+ *   context / buffers  src/examples.cpp:133-174 (create_vulkan_context),
+ *                      232-269 (create_host_buffer, upload_*, download_*),
+ *                      186-230 (destroy_buffer / destroy_vulkan_context)
+ *   st_launch          src/examples.cpp:271-448 (run_compute) and
+ *                      shaders/spirv_runtime.py:153-174 (run_spirv_kernel):
+ *                      a named kernel, a grid and ordered buffer bindings
+ *   st_vector_add      shaders/spirv_vector_add.py:44-92 (spirv_vector_add)
+ *   st_matmul          shaders/spirv_matmul.py:48-113 (spirv_matmul,
+ *                      cutile_matmul_spirv) and shaders/matmul.py:181-253
+ *                      (cutile_matmul)
+ *   *_host variants    the same calls on host memory, as the reference's
+ *                      Python API copies through the CPU (spirv_vector_add.py
+ *                      :37,89-92; spirv_runtime.py:162-173)
+ */
+#ifndef SPTILES_B200_H
+#define SPTILES_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes (replace VK_CHECK's std::runtime_error, examples.cpp:12-20) ---- */
+#define ST_OK 0
+#define ST_ERR_INVALID_ARGUMENT 1 /* bad shape, stride, dtype, size or null pointer */
+#define ST_ERR_UNKNOWN_ENTRY 2    /* no kernel registered under that entry name */
+#define ST_ERR_UNSUPPORTED 3      /* valid request this backend does not implement */
+#define ST_ERR_CUDA 4             /* a CUDA runtime/driver call failed */
+#define ST_ERR_NO_DEVICE 5        /* no usable sm_100 device */
+#define ST_ERR_OUT_OF_MEMORY 6
+#define ST_ERR_TIMEOUT 7          /* a bounded host wait ran out */
+#define ST_ERR_DEVICE_ABORT 8     /* a kernel's bounded on-device wait ran out */
+
+/* ---- element types ---- */
+#define ST_F32 0
+#define ST_F16 1
+#define ST_BF16 2
+#define ST_I32 3
+
+/* ---- binding kinds of st_param ---- */
+#define ST_PARAM_BUFFER 0 /* data pointer of one array (spirv StorageBuffer f32[]) */
+#define ST_PARAM_I32 1    /* one i32 scalar: a size, dim, stride or kernel constant */
+
+/* ---- st_exec.flags ---- */
+#define ST_EXEC_SYNC 1          /* block (bounded by timeout_ms) until the work is done */
+#define ST_EXEC_HOST_BUFFERS 2  /* st_launch only: buffer params are host memory */
+
+typedef struct st_ctx st_ctx;
+
+/* One binding of the cutile_python_v1 calling convention, in the reference's
+ * order: per 1D array (data, size, stride); per 2D array (data, dim0, dim1,
+ * stride0, stride1) (spirv_runtime.py:107-128; lower.hpp:197-209, 277-310).
+ * Trailing ST_PARAM_I32 entries after the arrays are the kernel's constants
+ * (tile sizes), as in ct.launch(..., (A, B, C, tm, tn, tk)) (matmul.py:252). */
+typedef struct {
+    int32_t kind;   /* ST_PARAM_BUFFER or ST_PARAM_I32 */
+    int32_t dtype;  /* buffer element type (ST_F32 / ST_F16 / ST_BF16) */
+    void *data;     /* buffer base address */
+    uint64_t bytes; /* buffer size in bytes; 0 = not checked */
+    int64_t value;  /* ST_PARAM_I32 value */
+} st_param;
+
+/* A tensor view: data + shape + strides in elements (rank 1 or 2). */
+typedef struct {
+    void *data;
+    int32_t dtype;
+    int32_t rank;
+    int64_t shape[2];
+    int64_t strides[2];
+} st_tensor;
+
+/* A cuda_tile grid: the number of tile blocks along each axis. */
+typedef struct {
+    uint32_t x, y, z;
+} st_grid;
+
+/* Where and how a call runs. */
+typedef struct {
+    void *stream;                  /* cudaStream_t; NULL = the context's own stream */
+    int32_t device;                /* CUDA ordinal; -1 = the context's first device */
+    int32_t flags;                 /* ST_EXEC_* */
+    uint32_t timeout_ms;           /* bound for ST_EXEC_SYNC waits; 0 = 60000 */
+    const int32_t *output_indices; /* ST_EXEC_HOST_BUFFERS: params copied back */
+    int32_t n_outputs;
+} st_exec;
+
+/* ---- library ---- */
+const char *st_version(void);
+const char *st_last_error(void);
+/* Number of CUDA devices visible to the process (0 when there is none). */
+int st_device_count(int32_t *count);
+/* Number of kernels this library has launched in the process so far. */
+int st_kernel_launches(uint64_t *count);
+
+/* ---- context: replaces create_vulkan_context / destroy_vulkan_context ---- */
+/* devices: CUDA ordinals to use (NULL with n_devices 0 = device 0). */
+int st_init(const int32_t *devices, int32_t n_devices, st_ctx **out);
+int st_shutdown(st_ctx *ctx);
+/* Bounded wait for all work the context issued on `device`; returns
+ * ST_ERR_TIMEOUT after timeout_ms, ST_ERR_DEVICE_ABORT if a kernel gave up
+ * a bounded wait. */
+int st_sync(st_ctx *ctx, int32_t device, uint32_t timeout_ms);
+/* The context's stream on `device` (a cudaStream_t). */
+int st_stream(st_ctx *ctx, int32_t device, void **stream);
+
+/* ---- device buffers: replace create_host_buffer / upload_* / download_* /
+ *      destroy_buffer (examples.cpp:186-269).  The caller owns them. ---- */
+int st_alloc(st_ctx *ctx, int32_t device, uint64_t bytes, void **out);
+int st_free(st_ctx *ctx, int32_t device, void *ptr);
+int st_upload(st_ctx *ctx, int32_t device, void *dst, const void *src, uint64_t bytes);
+int st_download(st_ctx *ctx, int32_t device, void *dst, const void *src, uint64_t bytes);
+
+/* ---- launch by entry name: replaces run_compute (examples.cpp:271-448) and
+ *      run_spirv_kernel (spirv_runtime.py:153-174).
+ * Registered entries (cuda_tile symbol names):
+ *   "vector_add"            A,B,C rank 1 f32 (9 params) [+ tile_size]       default tile 1024
+ *   "vector_add_2d"         A,B,C rank 2 f32 (15 params) [+ tile_m, tile_n]  default 64 x 64
+ *   "matmul_fp32", "matmul_f16", "matmul_bf16"
+ *                           A[M,K], B[K,N], C[M,N] rank 2 (15 params) [+ tm, tn, tk]
+ *   "matmul_fp32_bias", "matmul_f16_bias", "matmul_bf16_bias"
+ *                           as above + bias[N] rank 1 appended (18 params)
+ *   "persistent_matmul_fp32", "persistent_matmul_f16", "persistent_matmul_bf16"
+ *                           persistent-kernel semantics (matmul.py:106-178):
+ *                           any grid >= 1 covers every output tile
+ * grid counts tile blocks.  A matmul grid must cover every output tile
+ * (cdiv(M,tm)*cdiv(N,tn) blocks) unless the entry is persistent; a
+ * vector_add grid may cover fewer tiles, and only those are computed. */
+int st_launch(st_ctx *ctx, const char *entry_name, const st_grid *grid,
+              const st_param *params, int32_t n_params, const st_exec *exec);
+
+/* The reference runners dispatch workgroups of 1024 invocations, one output
+ * element each (lower.hpp:277-290; spirv_runtime.py:11).  Convert such a
+ * dispatch to the cuda_tile grid of `entry_name` with tile elements
+ * `tile_elems`: tiles = cdiv(dx*dy*dz*1024, tile_elems). */
+int st_grid_from_dispatch(const char *entry_name, const uint32_t dispatch[3], int64_t tile_elems,
+                          st_grid *out);
+
+/* ---- typed calls (device memory) ---- */
+/* C = A + B elementwise over the whole of C (rank 1 or 2, f32, any strides). */
+int st_vector_add(st_ctx *ctx, const st_tensor *a, const st_tensor *b, const st_tensor *c,
+                  const st_exec *exec);
+/* C[M,N] = A[M,K] @ B[K,N] (+ bias[N]); fp32 accumulation.  A and B are
+ * both f32 (3xTF32 on the tensor cores), both f16 or both bf16; C is f32,
+ * f16 or bf16; bias (may be NULL) is f32 or the input type. */
+int st_matmul(st_ctx *ctx, const st_tensor *a, const st_tensor *b, const st_tensor *bias,
+              const st_tensor *c, const st_exec *exec);
+
+/* ---- typed calls on host memory: copy in, compute, copy out, all on the
+ *      context's stream; returns once C is back in host memory. ---- */
+int st_vector_add_host(st_ctx *ctx, const st_tensor *a, const st_tensor *b, const st_tensor *c,
+                       const st_exec *exec);
+int st_matmul_host(st_ctx *ctx, const st_tensor *a, const st_tensor *b, const st_tensor *bias,
+                   const st_tensor *c, const st_exec *exec);
+
+/* ---- runtime policy, exposed for inspection and tests (no device work) ---- */
+/* Tile block (bid_m, bid_n) of tile id `bid` under the GROUP_SIZE_M raster
+ * of the cuTile matmul (matmul.py:14-24). */
+int st_tile_raster(int64_t m, int64_t n, int64_t tm, int64_t tn, int64_t group_m, int64_t bid,
+                   int64_t *bid_m, int64_t *bid_n);
+/* The tensor-core tile this runtime picks for a matmul: block_m x block_n x
+ * block_k elements, smem pipeline depth, and the CTA count of the persistent
+ * launch for a device with `sm_count` SMs. */
+int st_matmul_plan(int32_t in_dtype, int64_t m, int64_t n, int64_t k, int32_t sm_count,
+                   int32_t *block_m, int32_t *block_n, int32_t *block_k, int32_t *stages,
+                   int32_t *ctas);
+/* Contiguous shard [begin, end) of `total` units for `rank` of `count`
+ * ranks, boundaries rounded to multiples of `align` units (vector_add: 4
+ * elements = 16 bytes; matmul: M rows). */
+int st_shard_range(int64_t total, int32_t count, int32_t rank, int64_t align, int64_t *begin,
+                   int64_t *end);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SPTILES_B200_H */

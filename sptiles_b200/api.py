@@ -1,0 +1,193 @@
+"""Torch-facing operator API of the B200 backend.
+
+Same names, argument meaning and error behaviour as the reference's Python
+operators, so existing callers switch by changing an import:
+
+* ``spirv_vector_add``     shaders/spirv_vector_add.py:44-92
+* ``spirv_matmul``         shaders/spirv_matmul.py:48-98
+* ``cutile_matmul_spirv``  shaders/spirv_matmul.py:101-113
+* ``cutile_matmul``        shaders/matmul.py:181-253 (the cuTile host wrapper)
+
+Device (CUDA) tensors are used in place on torch's current stream; host
+tensors go through the C ABI's host-memory calls, which copy in, compute and
+copy out (the reference routes every call through the CPU,
+spirv_vector_add.py:37,89-92).  ``spirv_path`` is accepted and ignored: the
+kernels are native sm_100a code selected by ``entry_name``.
+"""
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+import torch
+
+from . import _native as N
+from .runtime import context
+
+VECTOR_ADD_TILE_SIZE = 16  # spirv_vector_add.py:27
+MATMUL_TILE_M = 32  # spirv_matmul.py:27
+MATMUL_TILE_N = 32  # spirv_matmul.py:28
+
+_CODES = {torch.float32: N.ST_F32, torch.float16: N.ST_F16, torch.bfloat16: N.ST_BF16}
+
+
+def dtype_code(dtype: torch.dtype) -> int:
+    try:
+        return _CODES[dtype]
+    except KeyError:
+        raise ValueError(f"unsupported dtype {dtype}") from None
+
+
+def tensor_view(t: torch.Tensor) -> N.StTensor:
+    """The C ABI view (data, dtype, rank, shape, strides) of a torch tensor."""
+    if t.dim() not in (1, 2):
+        raise ValueError("tensors must be rank 1 or 2")
+    v = N.StTensor()
+    v.data = t.data_ptr() if t.numel() else None
+    v.dtype = dtype_code(t.dtype)
+    v.rank = t.dim()
+    for i in range(t.dim()):
+        v.shape[i] = t.shape[i]
+        v.strides[i] = t.stride(i)
+    return v
+
+
+def _exec_for(t: torch.Tensor, flags: int = 0) -> N.StExec:
+    ex = N.StExec()
+    ex.flags = flags
+    ex.timeout_ms = 60000
+    if t.is_cuda:
+        ex.device = t.device.index if t.device.index is not None else torch.cuda.current_device()
+        ex.stream = torch.cuda.current_stream(t.device).cuda_stream
+    else:
+        ex.device = 0
+        ex.stream = None
+    return ex
+
+
+def _ctx(ex: N.StExec) -> int:
+    return context(ex.device)
+
+
+# ----------------------------------------------------------------- vector add
+def vector_add(A: torch.Tensor, B: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """C = A + B (f32, rank 1 or 2, any strides), bit-exact IEEE adds."""
+    if A.shape != B.shape:
+        raise ValueError(f"Input tensors must have the same shape: {A.shape} != {B.shape}")
+    if A.device != B.device:
+        raise ValueError("Input tensors must be on the same torch device.")
+    C = out if out is not None else torch.empty(A.shape, dtype=A.dtype, device=A.device,
+                                                 pin_memory=A.device.type == "cpu" and A.is_pinned())
+    ex = _exec_for(A)
+    va, vb, vc = tensor_view(A), tensor_view(B), tensor_view(C)
+    fn = N.lib().st_vector_add if A.is_cuda else N.lib().st_vector_add_host
+    N.check(fn(_ctx(ex), ctypes.byref(va), ctypes.byref(vb), ctypes.byref(vc), ctypes.byref(ex)), "vector_add")
+    return C
+
+
+def spirv_vector_add(A: torch.Tensor, B: torch.Tensor, *, spirv_path: str | Path | None = None,
+                     entry_name: str = "vector_add") -> torch.Tensor:
+    """Drop-in for the reference's spirv_vector_add (spirv_vector_add.py:44-92).
+
+    Checks the same preconditions with the same messages (equal shapes, same
+    device, 1D float32, size divisible by the exported tile size 16) and
+    returns the sum on the inputs' device.
+    """
+    if A.shape != B.shape:
+        raise ValueError(f"Input tensors must have the same shape: {A.shape} != {B.shape}")
+    if A.device != B.device:
+        raise ValueError("Input tensors must be on the same torch device.")
+    for t, name in ((A, "A"), (B, "B")):
+        if t.ndim != 1:
+            raise ValueError(f"{name} must be a 1D tensor.")
+        if t.dtype != torch.float32:
+            raise ValueError(f"{name} must be torch.float32; the current SPIR-V lowering is f32-only.")
+    if entry_name != "vector_add":
+        raise ValueError(f"Entry point {entry_name!r} was not found in the SPIR-V module.")
+    element_count = A.shape[0]
+    if element_count % VECTOR_ADD_TILE_SIZE != 0:
+        raise ValueError(f"vector_add expects a size divisible by {VECTOR_ADD_TILE_SIZE}; got {element_count}.")
+    return vector_add(A, B)
+
+
+# ----------------------------------------------------------------- matmul
+def matmul(A: torch.Tensor, B: torch.Tensor, bias: torch.Tensor | None = None, *,
+           out_dtype: torch.dtype | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """C = A @ B (+ bias) with fp32 accumulation on the tensor cores.
+
+    A, B: both float32 (3xTF32), both float16 or both bfloat16.  C defaults
+    to A's dtype (matmul.py:245); ``out_dtype`` may ask for float32, float16
+    or bfloat16.  bias (length N) is float32 or A's dtype.
+    """
+    if A.dim() != 2 or B.dim() != 2:
+        raise ValueError("A and B must be 2D tensors.")
+    if A.shape[1] != B.shape[0]:
+        raise ValueError(f"Incompatible matrices: K dimension of A ({A.shape[1]}) "
+                         f"must match K dimension of B ({B.shape[0]})")
+    if A.device != B.device or (bias is not None and bias.device != A.device):
+        raise ValueError("Input tensors must be on the same device.")
+    if A.dtype != B.dtype:
+        raise ValueError(f"A and B must have the same dtype ({A.dtype} != {B.dtype})")
+    m, n = A.shape[0], B.shape[1]
+    dt = out_dtype or A.dtype
+    if out is None:
+        out = torch.empty((m, n), dtype=dt, device=A.device,
+                          pin_memory=A.device.type == "cpu" and A.is_pinned())
+    ex = _exec_for(A)
+    va, vb, vc = tensor_view(A), tensor_view(B), tensor_view(out)
+    vbias = ctypes.byref(tensor_view(bias)) if bias is not None else None
+    fn = N.lib().st_matmul if A.is_cuda else N.lib().st_matmul_host
+    N.check(fn(_ctx(ex), ctypes.byref(va), ctypes.byref(vb), vbias, ctypes.byref(vc), ctypes.byref(ex)), "matmul")
+    return out
+
+
+def _check_spirv_matmul_args(A: torch.Tensor, B: torch.Tensor) -> None:
+    if A.shape[1] != B.shape[0]:
+        raise ValueError(f"Incompatible matrices: K dimension of A ({A.shape[1]}) "
+                         f"must match K dimension of B ({B.shape[0]})")
+    if A.device != B.device:
+        raise ValueError("Input tensors must be on the same torch device.")
+    for t, name in ((A, "A"), (B, "B")):
+        if t.ndim != 2:
+            raise ValueError(f"{name} must be a 2D tensor.")
+        if t.dtype != torch.float32:
+            raise ValueError(f"{name} must be torch.float32; the current SPIR-V lowering is f32-only.")
+
+
+def spirv_matmul(A: torch.Tensor, B: torch.Tensor, *, spirv_path: str | Path | None = None,
+                 entry_name: str = "matmul_fp32") -> torch.Tensor:
+    """Drop-in for the reference's spirv_matmul (spirv_matmul.py:48-98): fp32 C = A @ B."""
+    _check_spirv_matmul_args(A, B)
+    if entry_name not in ("matmul_fp32", "persistent_matmul_fp32"):
+        raise ValueError(f"Entry point {entry_name!r} was not found in the SPIR-V module.")
+    return matmul(A, B)
+
+
+def cutile_matmul_spirv(A: torch.Tensor, B: torch.Tensor, persistent: bool = False, *,
+                        spirv_path: str | Path | None = None, entry_name: str = "matmul_fp32") -> torch.Tensor:
+    """Drop-in for cutile_matmul_spirv (spirv_matmul.py:101-113).
+
+    The reference raises NotImplementedError for ``persistent=True``; here
+    the tensor-core kernel is persistent in every case, so both forms run and
+    give the same result.
+    """
+    return spirv_matmul(A, B, spirv_path=spirv_path,
+                        entry_name="persistent_matmul_fp32" if persistent else entry_name)
+
+
+def cutile_matmul(A: torch.Tensor, B: torch.Tensor, persistent: bool = False, *,
+                  bias: torch.Tensor | None = None, out_dtype: torch.dtype | None = None) -> torch.Tensor:
+    """Drop-in for the cuTile host wrapper cutile_matmul (matmul.py:181-253).
+
+    Same validation (K match, same device, CUDA tensors) and the same output
+    dtype rule (C takes A's dtype, matmul.py:245) unless ``out_dtype`` says
+    otherwise; tile shapes are chosen by the native runtime.
+    """
+    if A.shape[1] != B.shape[0]:
+        raise ValueError(f"Incompatible matrices: K dimension of A ({A.shape[1]}) "
+                         f"must match K dimension of B ({B.shape[0]})")
+    if A.device != B.device:
+        raise ValueError("Input tensors must be on the same device.")
+    if not A.is_cuda or not B.is_cuda:
+        raise ValueError("Input tensors must be on a CUDA device.")
+    return matmul(A, B, bias, out_dtype=out_dtype)

@@ -1,0 +1,109 @@
+// common.h -- shared host-side declarations of the runtime: status helpers,
+// the kernel launchers each .cu file provides, and tensor-view utilities.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <string>
+
+#include "../../include/sptiles_b200.h"
+
+namespace st {
+
+// Record `msg` as the calling thread's last error and return `code`.
+int fail(int code, const std::string &msg);
+// Map a CUDA error to ST_ERR_CUDA / ST_ERR_OUT_OF_MEMORY with a message.
+int cuda_fail(cudaError_t e, const char *what);
+
+#define ST_CUDA_TRY(expr)                                        \
+    do {                                                         \
+        cudaError_t st_e_ = (expr);                              \
+        if (st_e_ != cudaSuccess) return ::st::cuda_fail(st_e_, #expr); \
+    } while (0)
+
+#define ST_TRY(expr)                 \
+    do {                             \
+        int st_rc_ = (expr);         \
+        if (st_rc_ != ST_OK) return st_rc_; \
+    } while (0)
+
+inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+// Process-wide count of kernel launches issued by this library.
+void note_launch(uint64_t n = 1);
+
+inline size_t dtype_size(int dtype) {
+    switch (dtype) {
+    case ST_F32: return 4;
+    case ST_F16: return 2;
+    case ST_BF16: return 2;
+    case ST_I32: return 4;
+    default: return 0;
+    }
+}
+
+// Error word each kernel with bounded waits may set (one int per device).
+// Codes written by kernels:
+constexpr int kDevAbortGemmProducer = 0x101;
+constexpr int kDevAbortGemmMma = 0x102;
+constexpr int kDevAbortGemmEpilogue = 0x103;
+
+// ---- launchers (implemented in vecadd.cu, gemm.cu, pack.cu) ----
+
+// C[i] = A[i] + B[i] for i in [0, n), element strides sa, sb, sc.
+int launch_vector_add_1d(const float *a, int64_t sa, const float *b, int64_t sb, float *c, int64_t sc, int64_t n,
+                         int sm_count, cudaStream_t stream);
+// C[r, q] = A[r, q] + B[r, q] for r < rows, q < cols with 2D element strides.
+int launch_vector_add_2d(const float *a, const int64_t sa[2], const float *b, const int64_t sb[2], float *c,
+                         const int64_t sc[2], int64_t rows, int64_t cols, int sm_count, cudaStream_t stream);
+
+// Tensor-core GEMM plan.
+struct GemmPlan {
+    int block_m = 128;
+    int block_n = 256;
+    int block_k = 64;  // elements per pipeline stage (128 bytes of K)
+    int stages = 4;
+    int ctas = 148;
+    int tiles = 0;
+};
+
+int plan_gemm(int in_dtype, int64_t m, int64_t n, int64_t k, int sm_count, GemmPlan *plan);
+
+// D = A' B'^T-style tensor-core GEMM on operands already laid out for TMA:
+//   A: [M, K] row-major (K contiguous) of `ab_dtype` (ST_F16 / ST_BF16, or
+//      ST_F32 meaning tf32 operands), row stride lda elements.
+//   B: if b_k_major, [N, K] row-major (K contiguous), row stride ldb;
+//      else [K, N] row-major (N contiguous), row stride ldb.
+//   C: [M, N] with row stride ldc, element type c_dtype; bias[N] optional.
+struct GemmArgs {
+    int ab_dtype;
+    const void *a;
+    int64_t lda;
+    const void *b;
+    int64_t ldb;
+    bool b_k_major;
+    void *c;
+    int64_t ldc;
+    int c_dtype;
+    const void *bias;
+    int bias_dtype;
+    int64_t m, n, k;
+};
+int launch_gemm(const GemmArgs &args, int sm_count, int *dev_err, uint64_t timeout_ns, cudaStream_t stream);
+
+// 3xTF32 operand preparation.  x = hi + lo with hi, lo tf32-exact.
+//   A [M, K] (strides sa0, sa1) -> Ap [M, 3*kp] = [hi | hi | lo], kp = round_up(K, 32)
+//   B [K, N] (strides sb0, sb1) -> Bp [N, 3*kp] = [hi | lo | hi] (K contiguous)
+// so that Ap @ Bp^T = hi*hi + hi*lo + lo*hi.
+int64_t tf32_packed_k(int64_t k);
+int launch_pack_a_tf32(const float *a, int64_t sa0, int64_t sa1, int64_t m, int64_t k, float *ap, int64_t kp,
+                       cudaStream_t stream);
+int launch_pack_b_tf32(const float *b, int64_t sb0, int64_t sb1, int64_t k, int64_t n, float *bp, int64_t kp,
+                       cudaStream_t stream);
+// Copy a 16-bit [rows, cols] matrix with arbitrary element strides into a
+// dense row-major [rows, ld] buffer (ld >= cols, padding columns zeroed).
+int launch_repack_16(const uint16_t *src, int64_t s0, int64_t s1, int64_t rows, int64_t cols, uint16_t *dst,
+                     int64_t ld, cudaStream_t stream);
+
+}  // namespace st

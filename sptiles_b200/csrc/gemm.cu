@@ -1,0 +1,507 @@
+// gemm.cu -- the tiled mmaf matmul on the sm_100a tensor cores.
+//
+// Reference semantics (src/tileops.hpp:625-748 with the K-tile loop of
+// 859-1001, shaders/matmul.py:33-103): every output tile accumulates
+// A_tile @ B_tile over all K tiles in fp32 starting from zero, edge tiles
+// are zero padded, the accumulator is cast to C's type and stored with a
+// bounds check.  Here the same contraction runs as one persistent,
+// warp-specialised kernel per call:
+//
+//   warp 0      TMA producer: 128B-swizzled A and B tiles into a ring of
+//               shared-memory stages (zero fill at the edges gives the
+//               reference's padding for free)
+//   warp 1      MMA issuer: tcgen05.mma (kind::f16 for f16/bf16, kind::tf32
+//               for the 3xTF32 operands) into a TMEM accumulator; it also
+//               owns the TMEM allocation
+//   warps 2-5   epilogue: tcgen05.ld the accumulator, add the bias, convert,
+//               store with the reference's bounds check
+//
+// The TMEM accumulator is double buffered (2 x BLOCK_N columns) so the
+// epilogue of tile i overlaps the main loop of tile i+1.  Tiles are visited
+// in the GROUP_SIZE_M = 8 raster of matmul.py:14-24 for L2 reuse.
+// Every barrier wait is bounded; on time-out a role raises the CTA's abort
+// flag, records an error code in the device error word and unwinds.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+
+#include "common.h"
+#include "sm100.cuh"
+
+namespace st {
+
+// Tile raster of the cuTile matmul (matmul.py:14-24), shared by host and device.
+__host__ __device__ __forceinline__ void tile_raster(int64_t num_m, int64_t num_n, int64_t group_m, int64_t bid,
+                                                     int64_t &bm, int64_t &bn) {
+    const int64_t in_group = group_m * num_n;
+    const int64_t gid = bid / in_group;
+    const int64_t first_m = gid * group_m;
+    const int64_t rest = num_m - first_m;
+    const int64_t gsz = rest < group_m ? rest : group_m;
+    bm = first_m + (bid % gsz);
+    bn = (bid % in_group) / gsz;
+}
+
+namespace {
+
+constexpr int kBlockM = 128;
+constexpr int kRowBytes = 128;  // K bytes per stage row = one 128-byte swizzle span
+constexpr int kThreads = 192;   // 6 warps
+constexpr int kEpilogueWarps = 4;
+constexpr int kGroupM = 8;
+
+template <int BN>
+struct TileCfg {
+    static constexpr int kABytes = kBlockM * kRowBytes;
+    static constexpr int kBBytes = BN * kRowBytes;
+    static constexpr int kStageBytes = kABytes + kBBytes;
+    static constexpr int kStages = BN == 256 ? 4 : (BN == 128 ? 6 : 8);
+    static constexpr int kTmemCols = 2 * BN;  // two accumulators; 128, 256 or 512 (powers of two)
+    static constexpr int kBarBytes = 256;
+    static constexpr int kSmemBytes = kStages * kStageBytes + kBarBytes + 1024;  // + alignment slack
+};
+
+struct KParams {
+    int m, n, k;
+    int num_m_tiles, num_n_tiles, num_k_blocks, total_tiles;
+    void *c;
+    long long ldc;
+    int c_dtype;
+    const void *bias;
+    int bias_dtype;
+    int *err;
+    unsigned long long timeout_ns;
+};
+
+__device__ __forceinline__ float load_bias(const void *bias, int dtype, int i) {
+    if (dtype == ST_F32) return static_cast<const float *>(bias)[i];
+    if (dtype == ST_F16) return __half2float(static_cast<const __half *>(bias)[i]);
+    return __bfloat162float(static_cast<const __nv_bfloat16 *>(bias)[i]);
+}
+
+// Store 32 accumulator columns [col0, col0+32) of one row.
+__device__ __forceinline__ void store_row_chunk(const KParams &p, int row, int col0, const uint32_t (&r)[32]) {
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+    const int cnt = p.n - col0 < 32 ? p.n - col0 : 32;
+    if (p.bias != nullptr) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+            if (j < cnt) v[j] = __fadd_rn(v[j], load_bias(p.bias, p.bias_dtype, col0 + j));
+    }
+    const long long off = static_cast<long long>(row) * p.ldc + col0;
+    if (p.c_dtype == ST_F32) {
+        float *dst = static_cast<float *>(p.c) + off;
+        if (cnt == 32 && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4)
+                *reinterpret_cast<float4 *>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                if (j < cnt) dst[j] = v[j];
+        }
+    } else {
+        uint16_t h[32];
+        if (p.c_dtype == ST_F16) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) h[j] = __half_as_ushort(__float2half_rn(v[j]));
+        } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) h[j] = __bfloat16_as_ushort(__float2bfloat16_rn(v[j]));
+        }
+        uint16_t *dst = static_cast<uint16_t *>(p.c) + off;
+        if (cnt == 32 && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 8) {
+                uint4 q;
+                q.x = h[j] | (static_cast<uint32_t>(h[j + 1]) << 16);
+                q.y = h[j + 2] | (static_cast<uint32_t>(h[j + 3]) << 16);
+                q.z = h[j + 4] | (static_cast<uint32_t>(h[j + 5]) << 16);
+                q.w = h[j + 6] | (static_cast<uint32_t>(h[j + 7]) << 16);
+                *reinterpret_cast<uint4 *>(dst + j) = q;
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                if (j < cnt) dst[j] = h[j];
+        }
+    }
+}
+
+// FMT: 0 = f16, 1 = bf16, 2 = tf32.  B_MN: B tiles are N-contiguous.
+template <int FMT, bool B_MN, int BN>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                   const KParams p) {
+    using Cfg = TileCfg<BN>;
+    constexpr bool kTf32 = FMT == 2;
+    constexpr int kElem = kTf32 ? 4 : 2;
+    constexpr int kBK = kRowBytes / kElem;  // K elements per stage
+    constexpr int kMmaK = 32 / kElem;       // K elements per tcgen05.mma
+    constexpr int kKSteps = kBK / kMmaK;
+    constexpr uint32_t kIdesc = mma_idesc(FMT, false, B_MN, kBlockM, BN);
+    static_assert(!(kTf32 && B_MN), "tf32 operands are packed K-major");
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + Cfg::kStages * Cfg::kStageBytes);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * Cfg::kStages + 5);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t bar0 = smem_addr(bars);
+    auto full_bar = [&](int s) { return bar0 + 8u * s; };
+    auto empty_bar = [&](int s) { return bar0 + 8u * (Cfg::kStages + s); };
+    auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * Cfg::kStages + a); };
+    auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * Cfg::kStages + 2 + a); };
+    const uint32_t drain_bar = bar0 + 8u * (2 * Cfg::kStages + 4);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < Cfg::kStages; ++s) {
+            mbar_init(full_bar(s), 1);
+            mbar_init(empty_bar(s), 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(tfull_bar(a), 1);
+            mbar_init(tempty_bar(a), kEpilogueWarps);
+        }
+        mbar_init(drain_bar, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_map(&tmap_a);
+        tma_prefetch_map(&tmap_b);
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_addr(tmem_slot), Cfg::kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before_sync();
+    __syncthreads();
+    tc_fence_after_sync();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ------------------------------------------------ TMA producer
+        if (lane == 0) {
+            const uint64_t pol_a = l2_policy_evict_last();
+            const uint64_t pol_b = l2_policy_evict_last();
+            int s = 0;
+            uint32_t ph = 0;
+            uint32_t pending = 0;        // stages with a load in flight that nobody consumed yet
+            uint32_t pending_ph = 0;     // parity each pending load completes with
+            bool ok = true;
+            for (int t = blockIdx.x; ok && t < p.total_tiles; t += gridDim.x) {
+                int64_t tm, tn;
+                tile_raster(p.num_m_tiles, p.num_n_tiles, kGroupM, t, tm, tn);
+                const int m0 = static_cast<int>(tm) * kBlockM;
+                const int n0 = static_cast<int>(tn) * BN;
+                for (int kb = 0; kb < p.num_k_blocks; ++kb) {
+                    if (!mbar_wait(empty_bar(s), ph ^ 1u, abort_flag, p.timeout_ns)) {
+                        ok = false;
+                        break;
+                    }
+                    pending &= ~(1u << s);
+                    const uint32_t sa = smem_addr(smem + s * Cfg::kStageBytes);
+                    const uint32_t sb = sa + Cfg::kABytes;
+                    mbar_arrive_expect_tx(full_bar(s), Cfg::kStageBytes);
+                    tma_load_2d(sa, &tmap_a, full_bar(s), kb * kBK, m0, pol_a);
+                    if constexpr (B_MN) {
+#pragma unroll
+                        for (int j = 0; j < BN / 64; ++j)
+                            tma_load_2d(sb + j * (kBK * 128), &tmap_b, full_bar(s), n0 + 64 * j, kb * kBK, pol_b);
+                    } else {
+                        tma_load_2d(sb, &tmap_b, full_bar(s), kb * kBK, n0, pol_b);
+                    }
+                    pending |= 1u << s;
+                    pending_ph = (pending_ph & ~(1u << s)) | (ph << s);
+                    if (++s == Cfg::kStages) {
+                        s = 0;
+                        ph ^= 1u;
+                    }
+                }
+            }
+            if (!ok) {
+                *abort_flag = 1;
+                atomicExch(p.err, kDevAbortGemmProducer);
+                // let the loads already in flight land before the CTA exits
+                for (int q = 0; q < Cfg::kStages; ++q)
+                    if (pending & (1u << q))
+                        (void)mbar_wait(full_bar(q), (pending_ph >> q) & 1u, abort_flag, p.timeout_ns);
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            int s = 0;
+            uint32_t ph = 0;
+            int iter = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; ok && t < p.total_tiles; t += gridDim.x, ++iter) {
+                const int acc = iter & 1;
+                const uint32_t acc_ph = static_cast<uint32_t>(iter >> 1) & 1u;
+                if (!mbar_wait(tempty_bar(acc), acc_ph ^ 1u, abort_flag, p.timeout_ns)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after_sync();
+                const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+                for (int kb = 0; kb < p.num_k_blocks; ++kb) {
+                    if (!mbar_wait(full_bar(s), ph, abort_flag, p.timeout_ns)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after_sync();
+                    const uint32_t sa = smem_addr(smem + s * Cfg::kStageBytes);
+                    const uint32_t sb = sa + Cfg::kABytes;
+#pragma unroll
+                    for (int ks = 0; ks < kKSteps; ++ks) {
+                        // K-major operand: advance 32 bytes of K inside the swizzle row
+                        const uint64_t adesc = smem_desc_sw128(sa + ks * 32, 16, 1024);
+                        uint64_t bdesc;
+                        if constexpr (B_MN) {
+                            // N-contiguous operand: LBO = next 64-column chunk, SBO = next 8 K rows
+                            bdesc = smem_desc_sw128(sb + ks * (kMmaK * 128), kBK * 128, 1024);
+                        } else {
+                            bdesc = smem_desc_sw128(sb + ks * 32, 16, 1024);
+                        }
+                        tc_mma<kTf32>(d_tmem, adesc, bdesc, kIdesc, (kb | ks) != 0 ? 1u : 0u);
+                    }
+                    tc_commit(empty_bar(s));  // frees the stage when these MMAs retire
+                    if (++s == Cfg::kStages) {
+                        s = 0;
+                        ph ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                tc_commit(tfull_bar(acc));  // accumulator complete
+            }
+            if (!ok) {
+                *abort_flag = 1;
+                atomicExch(p.err, kDevAbortGemmMma);
+            }
+            // all MMAs issued by this thread have retired once drain_bar flips
+            tc_commit(drain_bar);
+            (void)mbar_wait(drain_bar, 0, abort_flag, p.timeout_ns);
+        }
+    } else {
+        // ------------------------------------------------ epilogue (warps 2..5)
+        const int g = warp & 3;  // TMEM lanes 32g..32g+31 are the ones this warp may read
+        int iter = 0;
+        for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x, ++iter) {
+            const int acc = iter & 1;
+            const uint32_t acc_ph = static_cast<uint32_t>(iter >> 1) & 1u;
+            int64_t tm, tn;
+            tile_raster(p.num_m_tiles, p.num_n_tiles, kGroupM, t, tm, tn);
+            const int m0 = static_cast<int>(tm) * kBlockM;
+            const int n0 = static_cast<int>(tn) * BN;
+            const bool ready = mbar_wait(tfull_bar(acc), acc_ph, abort_flag, p.timeout_ns);
+            if (!__all_sync(0xffffffffu, ready)) {
+                *abort_flag = 1;
+                if (lane == 0) atomicExch(p.err, kDevAbortGemmEpilogue);
+                break;
+            }
+            tc_fence_after_sync();
+            const int row = m0 + g * 32 + lane;
+            const uint32_t t_row = tmem_base + (static_cast<uint32_t>(g * 32) << 16) + static_cast<uint32_t>(acc * BN);
+#pragma unroll 1
+            for (int c = 0; c < BN / 32; ++c) {
+                uint32_t r[32];
+                tmem_load_32(t_row + c * 32, r);
+                tmem_load_wait();
+                const int col0 = n0 + c * 32;
+                if (row < p.m && col0 < p.n) store_row_chunk(p, row, col0, r);
+            }
+            tc_fence_before_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(tempty_bar(acc));
+        }
+    }
+
+    __syncthreads();
+    if (warp == 1) {
+        __syncwarp();
+        tc_fence_after_sync();
+        tmem_dealloc(tmem_base, Cfg::kTmemCols);
+    }
+}
+
+// ---------------------------------------------------------------- host side
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    });
+    return fn;
+}
+
+int make_map(CUtensorMap *map, CUtensorMapDataType dt, const void *base, uint64_t inner, uint64_t outer,
+             uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer) {
+    auto fn = encode_fn();
+    if (!fn) return fail(ST_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    cuuint64_t dims[2] = {inner, outer};
+    cuuint64_t strides[1] = {row_bytes};
+    cuuint32_t box[2] = {box_inner, box_outer};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, dt, 2, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return fail(ST_ERR_INVALID_ARGUMENT, "cuTensorMapEncodeTiled rejected an operand (error " +
+                                                 std::to_string(static_cast<int>(r)) + ")");
+    return ST_OK;
+}
+
+template <int FMT, bool B_MN, int BN>
+int launch_instance(const CUtensorMap &ma, const CUtensorMap &mb, const KParams &kp, int ctas, cudaStream_t stream) {
+    using Cfg = TileCfg<BN>;
+    auto kern = gemm_tc_kernel<FMT, B_MN, BN>;
+    static uint64_t attr_set = 0;  // one bit per device ordinal
+    int dev = 0;
+    ST_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64 || !(attr_set & (1ull << dev))) {
+        ST_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
+        if (dev >= 0 && dev < 64) attr_set |= 1ull << dev;
+    }
+    kern<<<ctas, kThreads, Cfg::kSmemBytes, stream>>>(ma, mb, kp);
+    note_launch();
+    const cudaError_t e = cudaPeekAtLastError();
+    return e == cudaSuccess ? ST_OK : cuda_fail(cudaGetLastError(), "gemm_tc_kernel launch");
+}
+
+template <int FMT, bool B_MN>
+int dispatch_bn(int bn, const CUtensorMap &ma, const CUtensorMap &mb, const KParams &kp, int ctas,
+                cudaStream_t stream) {
+    switch (bn) {
+    case 256: return launch_instance<FMT, B_MN, 256>(ma, mb, kp, ctas, stream);
+    case 128: return launch_instance<FMT, B_MN, 128>(ma, mb, kp, ctas, stream);
+    case 64: return launch_instance<FMT, B_MN, 64>(ma, mb, kp, ctas, stream);
+    default: return fail(ST_ERR_UNSUPPORTED, "unsupported block_n");
+    }
+}
+
+}  // namespace
+
+int plan_gemm(int in_dtype, int64_t m, int64_t n, int64_t k, int sm_count, GemmPlan *plan) {
+    if (m <= 0 || n <= 0 || k <= 0) return fail(ST_ERR_INVALID_ARGUMENT, "matmul extents must be positive");
+    if (sm_count <= 0) sm_count = 148;
+    GemmPlan best;
+    double best_score = -1.0;
+    // relative tensor-pipe efficiency of narrower MMA shapes (wider N reuses A better)
+    const int cand[3] = {256, 128, 64};
+    const double mma_eff[3] = {1.0, 0.93, 0.80};
+    for (int i = 0; i < 3; ++i) {
+        const int bn = cand[i];
+        const int64_t tiles = cdiv(m, kBlockM) * cdiv(n, bn);
+        const int64_t waves = cdiv(tiles, sm_count);
+        const double fill = static_cast<double>(tiles) / static_cast<double>(waves * sm_count);
+        // wasted columns of a partial last N tile
+        const double ncov = static_cast<double>(n) / static_cast<double>(cdiv(n, bn) * bn);
+        const double score = fill * ncov * mma_eff[i];
+        if (score > best_score + 1e-9) {
+            best_score = score;
+            best.block_n = bn;
+            best.tiles = static_cast<int>(tiles);
+        }
+    }
+    best.block_m = kBlockM;
+    best.block_k = in_dtype == ST_F32 ? 32 : 64;
+    best.stages = best.block_n == 256 ? TileCfg<256>::kStages
+                                      : (best.block_n == 128 ? TileCfg<128>::kStages : TileCfg<64>::kStages);
+    best.ctas = best.tiles < sm_count ? best.tiles : sm_count;
+    *plan = best;
+    return ST_OK;
+}
+
+int launch_gemm(const GemmArgs &g, int sm_count, int *dev_err, uint64_t timeout_ns, cudaStream_t stream) {
+    GemmPlan plan;
+    // the packed tf32 K already includes the 3x expansion; plan on the product extents
+    ST_TRY(plan_gemm(g.ab_dtype, g.m, g.n, g.k, sm_count, &plan));
+    const bool tf32 = g.ab_dtype == ST_F32;
+    const int elem = tf32 ? 4 : 2;
+    const int bk = kRowBytes / elem;
+    if (g.b_k_major == false && tf32) return fail(ST_ERR_UNSUPPORTED, "tf32 B operand must be K-major");
+    for (const void *p : {g.a, g.b})
+        if (reinterpret_cast<uintptr_t>(p) % 16 != 0)
+            return fail(ST_ERR_INVALID_ARGUMENT, "tensor-core operands must be 16-byte aligned");
+    if ((g.lda * elem) % 16 != 0 || (g.ldb * elem) % 16 != 0)
+        return fail(ST_ERR_INVALID_ARGUMENT, "tensor-core operand row strides must be multiples of 16 bytes");
+    const CUtensorMapDataType dt = tf32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                        : (g.ab_dtype == ST_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                                : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16);
+    CUtensorMap ma, mb;
+    ST_TRY(make_map(&ma, dt, g.a, static_cast<uint64_t>(g.k), static_cast<uint64_t>(g.m),
+                    static_cast<uint64_t>(g.lda) * elem, bk, kBlockM));
+    if (g.b_k_major) {
+        ST_TRY(make_map(&mb, dt, g.b, static_cast<uint64_t>(g.k), static_cast<uint64_t>(g.n),
+                        static_cast<uint64_t>(g.ldb) * elem, bk, plan.block_n));
+    } else {
+        ST_TRY(make_map(&mb, dt, g.b, static_cast<uint64_t>(g.n), static_cast<uint64_t>(g.k),
+                        static_cast<uint64_t>(g.ldb) * elem, 64, bk));
+    }
+    KParams kp;
+    kp.m = static_cast<int>(g.m);
+    kp.n = static_cast<int>(g.n);
+    kp.k = static_cast<int>(g.k);
+    kp.num_m_tiles = static_cast<int>(cdiv(g.m, kBlockM));
+    kp.num_n_tiles = static_cast<int>(cdiv(g.n, plan.block_n));
+    kp.num_k_blocks = static_cast<int>(cdiv(g.k, bk));
+    kp.total_tiles = kp.num_m_tiles * kp.num_n_tiles;
+    kp.c = g.c;
+    kp.ldc = g.ldc;
+    kp.c_dtype = g.c_dtype;
+    kp.bias = g.bias;
+    kp.bias_dtype = g.bias_dtype;
+    kp.err = dev_err;
+    kp.timeout_ns = timeout_ns;
+    if (g.ab_dtype == ST_F16) {
+        return g.b_k_major ? dispatch_bn<0, false>(plan.block_n, ma, mb, kp, plan.ctas, stream)
+                           : dispatch_bn<0, true>(plan.block_n, ma, mb, kp, plan.ctas, stream);
+    }
+    if (g.ab_dtype == ST_BF16) {
+        return g.b_k_major ? dispatch_bn<1, false>(plan.block_n, ma, mb, kp, plan.ctas, stream)
+                           : dispatch_bn<1, true>(plan.block_n, ma, mb, kp, plan.ctas, stream);
+    }
+    return dispatch_bn<2, false>(plan.block_n, ma, mb, kp, plan.ctas, stream);
+}
+
+}  // namespace st
+
+extern "C" int st_tile_raster(int64_t m, int64_t n, int64_t tm, int64_t tn, int64_t group_m, int64_t bid,
+                              int64_t *bid_m, int64_t *bid_n) {
+    if (m <= 0 || n <= 0 || tm <= 0 || tn <= 0 || group_m <= 0 || bid < 0 || !bid_m || !bid_n)
+        return st::fail(ST_ERR_INVALID_ARGUMENT, "st_tile_raster: extents must be positive");
+    const int64_t num_m = st::cdiv(m, tm), num_n = st::cdiv(n, tn);
+    if (bid >= num_m * num_n) return st::fail(ST_ERR_INVALID_ARGUMENT, "st_tile_raster: bid out of range");
+    st::tile_raster(num_m, num_n, group_m, bid, *bid_m, *bid_n);
+    return ST_OK;
+}
+
+extern "C" int st_matmul_plan(int32_t in_dtype, int64_t m, int64_t n, int64_t k, int32_t sm_count, int32_t *block_m,
+                              int32_t *block_n, int32_t *block_k, int32_t *stages, int32_t *ctas) {
+    if (in_dtype != ST_F32 && in_dtype != ST_F16 && in_dtype != ST_BF16)
+        return st::fail(ST_ERR_INVALID_ARGUMENT, "st_matmul_plan: in_dtype must be ST_F32, ST_F16 or ST_BF16");
+    st::GemmPlan plan;
+    const int64_t keff = in_dtype == ST_F32 ? 3 * st::tf32_packed_k(k) : k;
+    ST_TRY(st::plan_gemm(in_dtype, m, n, keff, sm_count, &plan));
+    if (block_m) *block_m = plan.block_m;
+    if (block_n) *block_n = plan.block_n;
+    if (block_k) *block_k = plan.block_k;
+    if (stages) *stages = plan.stages;
+    if (ctas) *ctas = plan.ctas;
+    return ST_OK;
+}

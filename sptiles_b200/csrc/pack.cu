@@ -1,0 +1,142 @@
+// pack.cu -- operand preparation for the tensor-core matmul.
+//
+// fp32 inputs: the reference computes the fp32 matmul at full precision
+// (its astype(tfloat32) lowers to identity, tileops.hpp:257-258).  The
+// tensor cores take tf32 (10 explicit mantissa bits), so each fp32 value is
+// split x = hi + lo with hi = tf32(x) and lo = tf32(x - hi), and the product
+// uses the three largest terms hi*hi + hi*lo + lo*hi -- the published
+// 3xTF32 method (CUTLASS's 3xTF32 GEMM; Ootomo & Yokota, "Recovering single
+// precision accuracy from Tensor Cores while surpassing the FP32 theoretical
+// peak performance", IJHPCA 2022).  Both halves are rounded to tf32 here, so
+// the tensor core's own handling of the discarded mantissa bits is moot.
+//
+// The three terms become ONE tf32 GEMM over a tripled K:
+//   Ap = [hi(A) | hi(A) | lo(A)]            [M, 3*kp], K contiguous
+//   Bp = [hi(B) ; lo(B) ; hi(B)]^T           [N, 3*kp], K contiguous
+// with kp = K rounded up to the 32-element stage depth (zero padded).
+//
+// 16-bit inputs whose strides TMA cannot address are copied into a dense
+// row-major scratch matrix first (repack_16).
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "common.h"
+
+namespace st {
+namespace {
+
+constexpr int kThreads = 256;
+
+// Round to tf32 (10 explicit mantissa bits), nearest-even; inf/nan unchanged.
+__device__ __forceinline__ float tf32_round(float x) {
+    uint32_t u = __float_as_uint(x);
+    if ((u & 0x7f800000u) == 0x7f800000u) return x;
+    u += 0x0fffu + ((u >> 13) & 1u);
+    return __uint_as_float(u & 0xffffe000u);
+}
+
+__global__ void __launch_bounds__(kThreads) pack_a_kernel(const float *__restrict__ a, int64_t sa0, int64_t sa1,
+                                                          int64_t m, int64_t k, float *__restrict__ ap,
+                                                          int64_t kp) {
+    // one thread per 4 consecutive k of one row
+    const int64_t groups = kp / 4;
+    const int64_t total = m * groups;
+    const int64_t step = static_cast<int64_t>(gridDim.x) * kThreads;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; i < total; i += step) {
+        const int64_t r = i / groups;
+        const int64_t k0 = (i - r * groups) * 4;
+        float hi[4], lo[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float x = (k0 + j < k) ? a[r * sa0 + (k0 + j) * sa1] : 0.0f;
+            hi[j] = tf32_round(x);
+            lo[j] = tf32_round(x - hi[j]);
+        }
+        float4 *row = reinterpret_cast<float4 *>(ap + r * 3 * kp);
+        const float4 h = make_float4(hi[0], hi[1], hi[2], hi[3]);
+        row[k0 / 4] = h;
+        row[(kp + k0) / 4] = h;
+        row[(2 * kp + k0) / 4] = make_float4(lo[0], lo[1], lo[2], lo[3]);
+    }
+}
+
+// B [K, N] -> Bp [N, 3*kp]: 32 x 32 tiles transposed through shared memory.
+__global__ void __launch_bounds__(kThreads) pack_b_kernel(const float *__restrict__ b, int64_t sb0, int64_t sb1,
+                                                          int64_t k, int64_t n, float *__restrict__ bp,
+                                                          int64_t kp) {
+    __shared__ float hi_t[32][33];
+    __shared__ float lo_t[32][33];
+    const int64_t k0 = static_cast<int64_t>(blockIdx.x) * 32;
+    const int64_t n0 = static_cast<int64_t>(blockIdx.y) * 32;
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8
+    for (int r = ty; r < 32; r += 8) {
+        const int64_t kk = k0 + r, nn = n0 + tx;
+        const float x = (kk < k && nn < n) ? b[kk * sb0 + nn * sb1] : 0.0f;
+        const float h = tf32_round(x);
+        hi_t[r][tx] = h;
+        lo_t[r][tx] = tf32_round(x - h);
+    }
+    __syncthreads();
+    for (int r = ty; r < 32; r += 8) {
+        const int64_t nn = n0 + r, kk = k0 + tx;
+        if (nn < n && kk < kp) {
+            float *row = bp + nn * 3 * kp;
+            const float h = hi_t[tx][r];
+            row[kk] = h;
+            row[kp + kk] = lo_t[tx][r];
+            row[2 * kp + kk] = h;
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kThreads) repack_16_kernel(const uint16_t *__restrict__ src, int64_t s0,
+                                                             int64_t s1, int64_t rows, int64_t cols,
+                                                             uint16_t *__restrict__ dst, int64_t ld) {
+    const int64_t total = rows * ld;
+    const int64_t step = static_cast<int64_t>(gridDim.x) * kThreads;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; i < total; i += step) {
+        const int64_t r = i / ld, c = i - r * ld;
+        dst[i] = c < cols ? src[r * s0 + c * s1] : static_cast<uint16_t>(0);
+    }
+}
+
+int grid_1d(int64_t items) {
+    int64_t g = cdiv(items, kThreads);
+    if (g > 148 * 16) g = 148 * 16;
+    return static_cast<int>(g > 0 ? g : 1);
+}
+
+}  // namespace
+
+int64_t tf32_packed_k(int64_t k) { return cdiv(k, 32) * 32; }
+
+int launch_pack_a_tf32(const float *a, int64_t sa0, int64_t sa1, int64_t m, int64_t k, float *ap, int64_t kp,
+                       cudaStream_t stream) {
+    if (m <= 0 || kp <= 0) return ST_OK;
+    pack_a_kernel<<<grid_1d(m * (kp / 4)), kThreads, 0, stream>>>(a, sa0, sa1, m, k, ap, kp);
+    note_launch();
+    const cudaError_t e = cudaPeekAtLastError();
+    return e == cudaSuccess ? ST_OK : cuda_fail(cudaGetLastError(), "pack_a_kernel");
+}
+
+int launch_pack_b_tf32(const float *b, int64_t sb0, int64_t sb1, int64_t k, int64_t n, float *bp, int64_t kp,
+                       cudaStream_t stream) {
+    if (n <= 0 || kp <= 0) return ST_OK;
+    dim3 grid(static_cast<unsigned>(cdiv(kp, 32)), static_cast<unsigned>(cdiv(n, 32)));
+    pack_b_kernel<<<grid, kThreads, 0, stream>>>(b, sb0, sb1, k, n, bp, kp);
+    note_launch();
+    const cudaError_t e = cudaPeekAtLastError();
+    return e == cudaSuccess ? ST_OK : cuda_fail(cudaGetLastError(), "pack_b_kernel");
+}
+
+int launch_repack_16(const uint16_t *src, int64_t s0, int64_t s1, int64_t rows, int64_t cols, uint16_t *dst,
+                     int64_t ld, cudaStream_t stream) {
+    if (rows <= 0 || ld <= 0) return ST_OK;
+    repack_16_kernel<<<grid_1d(rows * ld), kThreads, 0, stream>>>(src, s0, s1, rows, cols, dst, ld);
+    note_launch();
+    const cudaError_t e = cudaPeekAtLastError();
+    return e == cudaSuccess ? ST_OK : cuda_fail(cudaGetLastError(), "repack_16_kernel");
+}
+
+}  // namespace st

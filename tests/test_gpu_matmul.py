@@ -1,0 +1,257 @@
+"""The tensor-core matmul on the GPU against the oracle.
+
+Tolerance (relative to the largest reference magnitude of the matrix, since
+normal inputs make elementwise relative error meaningless near zero):
+  fp32 inputs (3xTF32):      max|C - C_ref| / max|C_ref| <= 1e-3
+  fp16 / bf16 inputs:        max|C - C_ref| / max|C_ref| <= 1e-2
+The reference's known-answer inputs make every partial sum exact, so those
+cases are compared bit for bit, at the benchmark configurations' full sizes
+as well.
+"""
+import ctypes
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+import sptiles_b200 as st
+from sptiles_b200 import _native as N
+
+pytestmark = pytest.mark.gpu
+
+GOLD = Path(__file__).resolve().parent / "golden"
+META = json.loads((GOLD / "golden.json").read_text())
+DEV = torch.device("cuda:0")
+TOL = {torch.float32: 1e-3, torch.float16: 1e-2, torch.bfloat16: 1e-2}
+
+
+def rel_err(got: np.ndarray, want: np.ndarray) -> float:
+    scale = float(np.max(np.abs(want))) or 1.0
+    return float(np.max(np.abs(got.astype(np.float64) - want.astype(np.float64)))) / scale
+
+
+def to_np(t: torch.Tensor) -> np.ndarray:
+    """Host numpy copy; bf16 as uint16 bit patterns (the oracle's convention)."""
+    t = t.detach().cpu().contiguous()
+    if t.dtype == torch.bfloat16:
+        return t.view(torch.int16).numpy().view(np.uint16)
+    return t.numpy()
+
+
+def as_f32(t: torch.Tensor) -> np.ndarray:
+    return t.detach().float().cpu().numpy()
+
+
+def oracle_mm(A, B, bias=None, rows=None, out=oracle.F32):
+    bf = A.dtype == torch.bfloat16
+    return oracle.matmul(to_np(A), to_np(B), None if bias is None else to_np(bias), bf16=bf, out_dtype=out,
+                         rows=rows)
+
+
+def kat(m, n, k, dtype):
+    a = oracle.kat_values(m * k, 17, 8, 0.25).reshape(m, k)
+    b = oracle.kat_values(k * n, 13, 6, 0.5).reshape(k, n)
+    return torch.from_numpy(a).to(DEV, dtype), torch.from_numpy(b).to(DEV, dtype)
+
+
+def normal(shape, std, seed, dtype):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    return (torch.randn(shape, generator=g) * std).to(dtype).to(DEV)
+
+
+# ------------------------------------------------------------ known answers
+@pytest.mark.parametrize("case", META["matmul"], ids=lambda c: c["file"])
+def test_known_answers_through_drop_in_api(case):
+    f = np.load(GOLD / case["file"])
+    A, B = torch.from_numpy(f["a"]), torch.from_numpy(f["b"])
+    C = st.spirv_matmul(A, B)  # host tensors, as the reference's main() (spirv_matmul.py:131-137)
+    assert C.device.type == "cpu" and C.dtype == torch.float32
+    assert C.numpy().tobytes() == f["expected"].tobytes()
+    Cp = st.cutile_matmul_spirv(A, B, persistent=True)
+    assert Cp.numpy().tobytes() == f["expected"].tobytes()
+
+
+@pytest.mark.parametrize("case", META["matmul"], ids=lambda c: c["file"])
+def test_known_answers_through_runner(case):
+    f = np.load(GOLD / case["file"])
+    m, n = case["m"], case["n"]
+    params = [*st.tensor_2d_descriptor(f["a"]), *st.tensor_2d_descriptor(f["b"]),
+              *st.tensor_2d_descriptor(np.zeros((m, n), np.float32))]
+    out = st.run_tile_kernel(entry_name="matmul_fp32", parameter_arrays=params, output_indices=[10],
+                             dispatch=tuple(case["dispatch"]))[0]
+    assert out.reshape(m, n).tobytes() == f["expected"].tobytes()
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("mnk", [(64, 64, 64), (256, 256, 256), (100, 70, 33), (33, 129, 200), (1, 1, 1),
+                                 (129, 257, 65), (1000, 24, 520)])
+def test_known_answers_all_dtypes(dtype, mnk):
+    m, n, k = mnk
+    A, B = kat(m, n, k, dtype)
+    C = st.matmul(A, B, out_dtype=torch.float32)
+    assert C.cpu().numpy().tobytes() == oracle.matmul_kat_expected(m, n, k).tobytes()
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_known_answers_full_size_8192_cube(dtype):
+    """The fp16 configuration's full size, every tile checked exactly."""
+    A, B = kat(8192, 8192, 8192, dtype)
+    C = st.matmul(A, B, out_dtype=torch.float32)
+    want = torch.from_numpy(oracle.matmul_kat_expected(8192, 8192, 8192)).to(DEV)
+    assert torch.equal(C, want)
+
+
+def test_known_answers_full_size_bias_config():
+    """M=32768, N=K=4096 bf16 with a fused bias: one rounding of (exact sum + bias)."""
+    m, n, k = 32768, 4096, 4096
+    A, B = kat(m, n, k, torch.bfloat16)
+    g = torch.Generator(device="cpu").manual_seed(4)
+    bias = (torch.rand(n, generator=g) * 2 - 1).to(torch.bfloat16)
+    exact = torch.from_numpy(oracle.matmul_kat_expected(m, n, k)).to(DEV)
+    want32 = exact + bias.to(DEV).float()  # fl(acc + bias), acc exact
+    C32 = st.matmul(A, B, bias.to(DEV), out_dtype=torch.float32)
+    assert torch.equal(C32, want32)
+    Cbf = st.matmul(A, B, bias.to(DEV))  # C takes A's dtype (matmul.py:245)
+    assert Cbf.dtype == torch.bfloat16
+    assert torch.equal(Cbf, want32.to(torch.bfloat16))
+
+
+# ------------------------------------------------------------ seeded random inputs
+def test_config_fp32_1024_cube_3xtf32():
+    A, B = normal((1024, 1024), 1.0, 2, torch.float32), normal((1024, 1024), 1.0, 20, torch.float32)
+    C = st.matmul(A, B)
+    want = oracle_mm(A, B)
+    err = rel_err(C.cpu().numpy(), want)
+    assert err <= 1e-3
+    assert err <= 1e-5, f"3xTF32 should be near fp32 accuracy, got {err}"
+
+
+def _sample_rows(m, block=128):
+    rows = []
+    for start in sorted({0, block, m // 2, m - block}):
+        rows.append((max(0, start), min(m, start + 8)))
+    return rows
+
+
+def test_config_fp16_8192_cube_sampled_rows():
+    m = n = k = 8192
+    A, B = normal((m, k), 0.1, 3, torch.float16), normal((k, n), 0.1, 30, torch.float16)
+    C = st.matmul(A, B, out_dtype=torch.float32)
+    for r0, r1 in _sample_rows(m):
+        want = oracle_mm(A, B, rows=(r0, r1))
+        assert rel_err(C[r0:r1].cpu().numpy(), want) <= 1e-2 * 0.1  # far inside the 1e-2 bound
+
+
+def test_config_bf16_bias_sampled_rows():
+    m, n, k = 32768, 4096, 4096
+    A, B = normal((m, k), 0.05, 4, torch.bfloat16), normal((k, n), 0.05, 40, torch.bfloat16)
+    g = torch.Generator(device="cpu").manual_seed(41)
+    bias = ((torch.rand(n, generator=g) * 2 - 1).to(torch.bfloat16)).to(DEV)
+    C = st.matmul(A, B, bias, out_dtype=torch.float32)
+    Cbf = st.matmul(A, B, bias)
+    for r0, r1 in _sample_rows(m):
+        want = oracle_mm(A, B, bias, rows=(r0, r1))
+        assert rel_err(C[r0:r1].cpu().numpy(), want) <= 1e-3
+        wbf = oracle_mm(A, B, bias, rows=(r0, r1), out=oracle.BF16)
+        got = to_np(Cbf[r0:r1])
+        assert rel_err(oracle.bf16_bits_to_f32(got), oracle.bf16_bits_to_f32(wbf)) <= 1e-2
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("mnk", [(5, 7, 3), (129, 257, 65), (300, 200, 1000), (256, 512, 128), (77, 1000, 40),
+                                 (1, 4096, 4096), (4096, 1, 300)])
+def test_random_ragged_shapes(dtype, mnk):
+    m, n, k = mnk
+    A, B = normal((m, k), 1.0, m + n, dtype), normal((k, n), 1.0, k, dtype)
+    C = st.matmul(A, B, out_dtype=torch.float32)
+    assert rel_err(C.cpu().numpy(), oracle_mm(A, B)) <= TOL[dtype]
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16, torch.float32])
+def test_operand_layouts(dtype):
+    """Transposed B (K-major path), strided A and B (repack path), padded C rows."""
+    m, n, k = 200, 136, 72
+    A = normal((m, k), 1.0, 1, dtype)
+    B = normal((k, n), 1.0, 2, dtype)
+    want = oracle_mm(A, B)
+    Bt = B.t().contiguous().t()  # column-major B
+    assert rel_err(st.matmul(A, Bt, out_dtype=torch.float32).cpu().numpy(), want) <= TOL[dtype]
+    Abig = normal((m, 2 * k), 1.0, 3, dtype)
+    Abig[:, ::2] = A
+    As = Abig[:, ::2]  # column stride 2
+    Bbig = torch.zeros((k, n + 3), dtype=dtype, device=DEV)
+    Bbig[:, :n] = B
+    Bs = Bbig[:, :n]  # row stride not a multiple of 16 bytes
+    out = torch.full((m, n + 8), 5.0, device=DEV)
+    st.matmul(As, Bs, out=out[:, :n])
+    assert rel_err(out[:, :n].cpu().numpy(), want) <= TOL[dtype]
+    assert torch.all(out[:, n:] == 5.0)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("out_dtype", [torch.float32, torch.float16, torch.bfloat16])
+def test_output_dtypes_and_bias(dtype, out_dtype):
+    m, n, k = 384, 640, 256
+    A, B = normal((m, k), 0.5, 5, dtype), normal((k, n), 0.5, 6, dtype)
+    for bias_dtype in (torch.float32, dtype):
+        bias = normal((n,), 1.0, 7, bias_dtype)
+        C = st.matmul(A, B, bias, out_dtype=out_dtype)
+        code = {torch.float32: oracle.F32, torch.float16: oracle.F16, torch.bfloat16: oracle.BF16}[out_dtype]
+        want = oracle_mm(A, B, bias, out=code)
+        got = to_np(C)
+        if out_dtype == torch.bfloat16:
+            got, want = oracle.bf16_bits_to_f32(got), oracle.bf16_bits_to_f32(want)
+        assert rel_err(np.asarray(got, np.float32), np.asarray(want, np.float32)) <= 1e-2
+
+
+def test_empty_contraction_gives_bias():
+    A = torch.zeros((5, 0), device=DEV, dtype=torch.float16)
+    B = torch.zeros((0, 7), device=DEV, dtype=torch.float16)
+    bias = torch.arange(7, device=DEV, dtype=torch.float32)
+    C = st.matmul(A, B, bias, out_dtype=torch.float32)
+    assert torch.equal(C, bias.expand(5, 7))
+    assert st.matmul(A, B, out_dtype=torch.float32).abs().sum() == 0
+
+
+def _launch_matmul(entry, grid, A, B, C, consts=()):
+    P = (N.StParam * (15 + len(consts)))()
+    i = 0
+    for t in (A, B, C):
+        P[i].kind, P[i].dtype, P[i].data, P[i].bytes = N.ST_PARAM_BUFFER, st.api.dtype_code(t.dtype), \
+            t.data_ptr(), t.numel() * t.element_size()
+        vals = [t.shape[0], t.shape[1], t.stride(0), t.stride(1)]
+        for j, v in enumerate(vals):
+            P[i + 1 + j].kind, P[i + 1 + j].value = N.ST_PARAM_I32, v
+        i += 5
+    for c in consts:
+        P[i].kind, P[i].value = N.ST_PARAM_I32, c
+        i += 1
+    g = N.StGrid(*grid)
+    ex = N.StExec(torch.cuda.current_stream().cuda_stream, 0, N.ST_EXEC_SYNC, 60000, None, 0)
+    N.check(N.lib().st_launch(st.context(0), entry.encode(), ctypes.byref(g), P, len(P), ctypes.byref(ex)), entry)
+
+
+def test_persistent_entry_any_grid_and_grid_coverage_rule():
+    m, n, k = 512, 384, 256
+    A, B = kat(m, n, k, torch.float16)
+    want = torch.from_numpy(oracle.matmul_kat_expected(m, n, k)).to(DEV)
+    for grid in (1, 7, 148):
+        C = torch.zeros((m, n), device=DEV)
+        _launch_matmul("persistent_matmul_f16", (grid, 1, 1), A, B, C)
+        assert torch.equal(C, want)
+    C = torch.zeros((m, n), device=DEV)
+    tiles = (m // 128) * -(-n // 256)
+    _launch_matmul("matmul_f16", (tiles, 1, 1), A, B, C, consts=(128, 256, 64))
+    assert torch.equal(C, want)
+    with pytest.raises(NotImplementedError, match="cover"):
+        _launch_matmul("matmul_f16", (tiles - 1, 1, 1), A, B, C, consts=(128, 256, 64))
+
+
+def test_entry_dtype_mismatch_is_rejected():
+    A, B = kat(64, 64, 64, torch.float16)
+    C = torch.zeros((64, 64), device=DEV)
+    with pytest.raises(ValueError, match="dtype"):
+        _launch_matmul("matmul_bf16", (4, 1, 1), A, B, C)
