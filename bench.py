@@ -522,8 +522,12 @@ def main():
         secondary = None
         if args.workload == "matmul_f16" and not args.no_secondary:
             vw = WORKLOADS["vector_add_2d"]
-            sub = run_vector_add(vw, args, rank, world, local, dist_on, peaks)
+            # a ~35 us step needs more steps for a timed region the clock sampler can see
+            sub_args = argparse.Namespace(**{**vars(args), "steps": max(args.steps, 1000),
+                                             "warmup": max(args.warmup, 10)})
+            sub = run_vector_add(vw, sub_args, rank, world, local, dist_on, peaks)
             secondary = {"workload": "vector_add_2d", "value": round(sub["value"], 1), "unit": "GB/s",
+                         "steps": sub_args.steps, "warmup": sub_args.warmup,
                          "ms_per_step": round(sub["ms_per_step"], 5), "roofline": sub["roofline"],
                          "e2e": sub.get("e2e"), "gpu_launches": sub["gpu_launches"], "clocks": sub["clocks"],
                          "config": config_of("vector_add_2d", vw, world)}

@@ -88,7 +88,8 @@ typedef struct {
 
 /* Where and how a call runs. */
 typedef struct {
-    void *stream;                  /* cudaStream_t; NULL = the context's own stream */
+    void *stream;                  /* cudaStream_t; NULL = the context's own stream
+                                      (pass cudaStreamLegacy, 0x1, for the NULL stream) */
     int32_t device;                /* CUDA ordinal; -1 = the context's first device */
     int32_t flags;                 /* ST_EXEC_* */
     uint32_t timeout_ms;           /* bound for ST_EXEC_SYNC waits; 0 = 60000 */

@@ -28,6 +28,8 @@ VECTOR_ADD_TILE_SIZE = 16  # spirv_vector_add.py:27
 MATMUL_TILE_M = 32  # spirv_matmul.py:27
 MATMUL_TILE_N = 32  # spirv_matmul.py:28
 
+CUDA_STREAM_LEGACY = 0x1  # cudaStreamLegacy: the implicitly synchronising NULL stream
+
 _CODES = {torch.float32: N.ST_F32, torch.float16: N.ST_F16, torch.bfloat16: N.ST_BF16}
 
 
@@ -58,7 +60,10 @@ def _exec_for(t: torch.Tensor, flags: int = 0) -> N.StExec:
     ex.timeout_ms = 60000
     if t.is_cuda:
         ex.device = t.device.index if t.device.index is not None else torch.cuda.current_device()
-        ex.stream = torch.cuda.current_stream(t.device).cuda_stream
+        handle = torch.cuda.current_stream(t.device).cuda_stream
+        # torch's default stream is the legacy NULL stream; NULL would select
+        # the context's own stream, so name it explicitly (cudaStreamLegacy)
+        ex.stream = handle if handle else CUDA_STREAM_LEGACY
     else:
         ex.device = 0
         ex.stream = None
