@@ -165,6 +165,24 @@ int st_vector_add_host(st_ctx *ctx, const st_tensor *a, const st_tensor *b, cons
 int st_matmul_host(st_ctx *ctx, const st_tensor *a, const st_tensor *b, const st_tensor *bias,
                    const st_tensor *c, const st_exec *exec);
 
+/* ---- fp32 matmul that allocates nothing ----
+ * No counterpart in the reference.  For callers that must not allocate
+ * device memory: a process whose memory pool already holds the GPU's memory,
+ * or a latency-critical caller that cannot pay for cudaMalloc / cudaFree
+ * (cudaFree waits for the whole device).  Same arithmetic as st_matmul with
+ * f32 A and B (3xTF32), but the packed operands live in one fixed
+ * ST_STATIC_SCRATCH_BYTES device array inside the library, which every GPU
+ * that loads the library holds until the process exits.  Needs no context:
+ * exec may be NULL; exec->stream NULL means the legacy default stream.
+ *   - (M + N) * 3 * roundup(K, 32) * 4 bytes must fit in the array, else
+ *     ST_ERR_INVALID_ARGUMENT; bias, if given, is f32.
+ *   - The first call on a device finds the array's device address (set-up);
+ *     make that first call before any stream capture.
+ *   - All calls share the array: calls that overlap on the GPU race. */
+#define ST_STATIC_SCRATCH_BYTES (32u * 1024u * 1024u)
+int st_matmul_static_scratch(const st_tensor *a, const st_tensor *b, const st_tensor *bias, const st_tensor *c,
+                             const st_exec *exec);
+
 /* ---- runtime policy, exposed for inspection and tests (no device work) ---- */
 /* Tile block (bid_m, bid_n) of tile id `bid` under the GROUP_SIZE_M raster
  * of the cuTile matmul (matmul.py:14-24). */
