@@ -60,6 +60,7 @@ int launch_vector_add_2d(const float *a, const int64_t sa[2], const float *b, co
 
 // Tensor-core GEMM plan.
 struct GemmPlan {
+    bool pair = false;  // CTA-pair kernel (cta_group::2): block_m 256, block_n 256
     int block_m = 128;
     int block_n = 256;
     int block_k = 64;  // elements per pipeline stage (128 bytes of K)

@@ -28,6 +28,8 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -336,6 +338,245 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
+// ---------------------------------------------------------------- CTA-pair kernel
+// Two CTAs of a cluster (one TPC) share one 256 x 256 output tile: each
+// stages 128 rows of A and 128 columns of B per K step, and the even CTA
+// issues tcgen05.mma.cta_group::2, which reads both CTAs' shared memory and
+// writes rows 0-127 of the accumulator into its own TMEM and rows 128-255
+// into its partner's.  Per SM this halves the B bytes staged and read per
+// MMA compared with the one-CTA kernel.
+//
+// Signalling between the two CTAs (no multicast anywhere):
+//   full[s]   lives in the even CTA; both CTAs' TMA loads complete on it
+//             (cta_group::2 form), the even producer arrives with the
+//             pair's byte count.
+//   empty[s]  the even CTA's MMA commit frees its own stage; its producer,
+//             having seen that, arrives remotely on the odd CTA's empty[s].
+//   tfull[a]  the commit completes the even CTA's barrier; its first
+//             epilogue warp forwards it to the odd CTA's tfull[a].
+//   tempty[a] lives in the even CTA and counts all 8 epilogue warps of the
+//             pair (the odd CTA's arrive remotely).
+constexpr int kPairN = 256;      // N of one pair MMA
+constexpr int kPairHalfN = 128;  // columns of B each CTA stages
+
+struct PairCfg {
+    static constexpr int kABytes = kBlockM * kRowBytes;
+    static constexpr int kBBytes = kPairHalfN * kRowBytes;
+    static constexpr int kStageBytes = kABytes + kBBytes;
+    static constexpr int kStages = 6;
+    static constexpr int kTmemCols = 512;  // two 256-column accumulators
+    static constexpr int kSmemBytes = kStages * kStageBytes + 256 + 1024;
+};
+
+template <int FMT, bool B_MN>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                        const KParams p) {
+    using Cfg = PairCfg;
+    constexpr bool kTf32 = FMT == 2;
+    constexpr int kElem = kTf32 ? 4 : 2;
+    constexpr int kBK = kRowBytes / kElem;
+    constexpr int kMmaK = 32 / kElem;
+    constexpr int kKSteps = kBK / kMmaK;
+    constexpr uint32_t kIdesc = mma_idesc(FMT, false, B_MN, 2 * kBlockM, kPairN);
+    static_assert(!(kTf32 && B_MN), "tf32 operands are packed K-major");
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + Cfg::kStages * Cfg::kStageBytes);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * Cfg::kStages + 5);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_rank();
+    const bool even = rank == 0;
+    const int pair = static_cast<int>(blockIdx.x >> 1);
+    const int num_pairs = static_cast<int>(gridDim.x >> 1);
+    const uint32_t bar0 = smem_addr(bars);
+    auto full_bar = [&](int s) { return bar0 + 8u * s; };
+    auto empty_bar = [&](int s) { return bar0 + 8u * (Cfg::kStages + s); };
+    auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * Cfg::kStages + a); };
+    auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * Cfg::kStages + 2 + a); };
+    const uint32_t drain_bar = bar0 + 8u * (2 * Cfg::kStages + 4);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < Cfg::kStages; ++s) {
+            mbar_init(full_bar(s), 1);
+            mbar_init(empty_bar(s), 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(tfull_bar(a), 1);
+            mbar_init(tempty_bar(a), 2 * kEpilogueWarps);
+        }
+        mbar_init(drain_bar, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_map(&tmap_a);
+        tma_prefetch_map(&tmap_b);
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(smem_addr(tmem_slot), Cfg::kTmemCols);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before_sync();
+    cluster_sync();  // barriers of both CTAs initialised, TMEM allocated
+    tc_fence_after_sync();
+    const uint32_t tmem_base = *tmem_slot;
+    const uint32_t even_full0 = map_to_rank(full_bar(0), 0);  // full[s] of the even CTA: + 8 s
+
+    const int num_m_pairs = (p.m + 2 * kBlockM - 1) / (2 * kBlockM);
+    const int num_n_pairs = (p.n + kPairN - 1) / kPairN;
+    const int total = num_m_pairs * num_n_pairs;
+
+    if (warp == 0) {
+        // ------------------------------------------------ TMA producer (both CTAs)
+        if (lane == 0) {
+            const uint64_t pol = l2_policy_evict_last();
+            int s = 0;
+            uint32_t ph = 0;
+            int round = 0;  // passes over the ring completed
+            bool ok = true;
+            for (int t = pair; ok && t < total; t += num_pairs) {
+                int64_t tm, tn;
+                tile_raster(num_m_pairs, num_n_pairs, kGroupM, t, tm, tn);
+                const int m0 = static_cast<int>(tm) * 2 * kBlockM + static_cast<int>(rank) * kBlockM;
+                const int n0 = static_cast<int>(tn) * kPairN + static_cast<int>(rank) * kPairHalfN;
+                for (int kb = 0; kb < p.num_k_blocks; ++kb) {
+                    if (!mbar_wait(empty_bar(s), ph ^ 1u, abort_flag, p.timeout_ns)) {
+                        ok = false;
+                        break;
+                    }
+                    if (even) {
+                        if (round > 0) mbar_arrive_cluster(map_to_rank(empty_bar(s), 1));  // stage free for the odd CTA
+                        mbar_arrive_expect_tx(full_bar(s), 2 * Cfg::kStageBytes);
+                    }
+                    const uint32_t sa = smem_addr(smem + s * Cfg::kStageBytes);
+                    const uint32_t sb = sa + Cfg::kABytes;
+                    const uint32_t fb = even_full0 + 8u * s;
+                    tma_load_2d_pair(sa, &tmap_a, fb, kb * kBK, m0, pol);
+                    if constexpr (B_MN) {
+#pragma unroll
+                        for (int j = 0; j < kPairHalfN / 64; ++j)
+                            tma_load_2d_pair(sb + j * (kBK * 128), &tmap_b, fb, n0 + 64 * j, kb * kBK, pol);
+                    } else {
+                        tma_load_2d_pair(sb, &tmap_b, fb, kb * kBK, n0, pol);
+                    }
+                    if (++s == Cfg::kStages) {
+                        s = 0;
+                        ph ^= 1u;
+                        ++round;
+                    }
+                }
+            }
+            if (!ok) {
+                *abort_flag = 1;
+                atomicExch(p.err, kDevAbortGemmProducer);
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------ MMA issuer (even CTA)
+        if (even && lane == 0) {
+            int s = 0;
+            uint32_t ph = 0;
+            int iter = 0;
+            bool ok = true;
+            for (int t = pair; ok && t < total; t += num_pairs, ++iter) {
+                const int acc = iter & 1;
+                const uint32_t acc_ph = static_cast<uint32_t>(iter >> 1) & 1u;
+                if (!mbar_wait(tempty_bar(acc), acc_ph ^ 1u, abort_flag, p.timeout_ns)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after_sync();
+                const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kPairN);
+                for (int kb = 0; kb < p.num_k_blocks; ++kb) {
+                    if (!mbar_wait(full_bar(s), ph, abort_flag, p.timeout_ns)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after_sync();
+                    const uint32_t sa = smem_addr(smem + s * Cfg::kStageBytes);
+                    const uint32_t sb = sa + Cfg::kABytes;
+#pragma unroll
+                    for (int ks = 0; ks < kKSteps; ++ks) {
+                        const uint64_t adesc = smem_desc_sw128(sa + ks * 32, 16, 1024);
+                        uint64_t bdesc;
+                        if constexpr (B_MN) {
+                            bdesc = smem_desc_sw128(sb + ks * (kMmaK * 128), kBK * 128, 1024);
+                        } else {
+                            bdesc = smem_desc_sw128(sb + ks * 32, 16, 1024);
+                        }
+                        tc_mma_pair<kTf32>(d_tmem, adesc, bdesc, kIdesc, (kb | ks) != 0 ? 1u : 0u);
+                    }
+                    tc_commit_pair(empty_bar(s));
+                    if (++s == Cfg::kStages) {
+                        s = 0;
+                        ph ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                tc_commit_pair(tfull_bar(acc));
+            }
+            if (!ok) {
+                *abort_flag = 1;
+                atomicExch(p.err, kDevAbortGemmMma);
+            }
+            tc_commit_pair(drain_bar);
+            (void)mbar_wait(drain_bar, 0, abort_flag, p.timeout_ns);
+        }
+    } else {
+        // ------------------------------------------------ epilogue (warps 2..5, both CTAs)
+        const int g = warp & 3;
+        const uint32_t even_tempty0 = map_to_rank(tempty_bar(0), 0);
+        const uint32_t odd_tfull0 = map_to_rank(tfull_bar(0), 1);
+        int iter = 0;
+        for (int t = pair; t < total; t += num_pairs, ++iter) {
+            const int acc = iter & 1;
+            const uint32_t acc_ph = static_cast<uint32_t>(iter >> 1) & 1u;
+            int64_t tm, tn;
+            tile_raster(num_m_pairs, num_n_pairs, kGroupM, t, tm, tn);
+            const int m0 = static_cast<int>(tm) * 2 * kBlockM + static_cast<int>(rank) * kBlockM;
+            const int n0 = static_cast<int>(tn) * kPairN;
+            const bool ready = mbar_wait(tfull_bar(acc), acc_ph, abort_flag, p.timeout_ns);
+            if (!__all_sync(0xffffffffu, ready)) {
+                *abort_flag = 1;
+                if (lane == 0) atomicExch(p.err, kDevAbortGemmEpilogue);
+                break;
+            }
+            if (even && warp == 2 && lane == 0) mbar_arrive_cluster(odd_tfull0 + 8u * acc);
+            tc_fence_after_sync();
+            const int row = m0 + g * 32 + lane;
+            const uint32_t t_row =
+                tmem_base + (static_cast<uint32_t>(g * 32) << 16) + static_cast<uint32_t>(acc * kPairN);
+#pragma unroll 1
+            for (int c = 0; c < kPairN / 32; ++c) {
+                uint32_t r[32];
+                tmem_load_32(t_row + c * 32, r);
+                tmem_load_wait();
+                const int col0 = n0 + c * 32;
+                if (row < p.m && col0 < p.n) store_row_chunk(p, row, col0, r);
+            }
+            tc_fence_before_sync();
+            __syncwarp();
+            if (lane == 0) {
+                if (even) mbar_arrive(tempty_bar(acc));
+                else mbar_arrive_cluster(even_tempty0 + 8u * acc);
+            }
+        }
+    }
+
+    tc_fence_before_sync();
+    cluster_sync();  // all MMAs retired, all TMEM reads done, no remote access pending
+    if (warp == 1) {
+        __syncwarp();
+        tc_fence_after_sync();
+        tmem_dealloc_pair(tmem_base, Cfg::kTmemCols);
+    }
+}
+
 // ---------------------------------------------------------------- host side
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -394,35 +635,107 @@ int dispatch_bn(int bn, const CUtensorMap &ma, const CUtensorMap &mb, const KPar
     }
 }
 
+template <int FMT, bool B_MN>
+int launch_pair(const CUtensorMap &ma, const CUtensorMap &mb, const KParams &kp, int pairs_wanted,
+                cudaStream_t stream) {
+    auto kern = gemm_tc_pair_kernel<FMT, B_MN>;
+    static uint64_t attr_set = 0;
+    static int max_clusters[64] = {0};
+    int dev = 0;
+    ST_CUDA_TRY(cudaGetDevice(&dev));
+    const bool cached = dev >= 0 && dev < 64 && (attr_set & (1ull << dev));
+    int clusters = cached ? max_clusters[dev] : 0;
+    if (!cached) {
+        ST_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, PairCfg::kSmemBytes));
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(2 * pairs_wanted, 1, 1);
+        cfg.blockDim = dim3(kThreads, 1, 1);
+        cfg.dynamicSmemBytes = PairCfg::kSmemBytes;
+        cudaLaunchAttribute attr;
+        attr.id = cudaLaunchAttributeClusterDimension;
+        attr.val.clusterDim.x = 2;
+        attr.val.clusterDim.y = 1;
+        attr.val.clusterDim.z = 1;
+        cfg.attrs = &attr;
+        cfg.numAttrs = 1;
+        if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) != cudaSuccess || clusters <= 0) {
+            cudaGetLastError();
+            clusters = pairs_wanted;
+        }
+        if (dev >= 0 && dev < 64) {
+            max_clusters[dev] = clusters;
+            attr_set |= 1ull << dev;
+        }
+    }
+    const int pairs = pairs_wanted < clusters ? pairs_wanted : clusters;
+    if (std::getenv("SPTILES_B200_DEBUG"))
+        std::fprintf(stderr, "[sptiles_b200] pair gemm: %d pairs (wanted %d, co-resident clusters %d), smem %d\n",
+                     pairs, pairs_wanted, clusters, PairCfg::kSmemBytes);
+    kern<<<2 * pairs, kThreads, PairCfg::kSmemBytes, stream>>>(ma, mb, kp);
+    note_launch();
+    const cudaError_t e = cudaPeekAtLastError();
+    return e == cudaSuccess ? ST_OK : cuda_fail(cudaGetLastError(), "gemm_tc_pair_kernel launch");
+}
+
 }  // namespace
 
 int plan_gemm(int in_dtype, int64_t m, int64_t n, int64_t k, int sm_count, GemmPlan *plan) {
     if (m <= 0 || n <= 0 || k <= 0) return fail(ST_ERR_INVALID_ARGUMENT, "matmul extents must be positive");
     if (sm_count <= 0) sm_count = 148;
+    // SPTILES_B200_GEMM_KERNEL=pair|single pins the kernel family (tests use it
+    // to cover both on every shape); unset, the scores below decide
+    const char *force = std::getenv("SPTILES_B200_GEMM_KERNEL");
+    const bool only_pair = force && std::strcmp(force, "pair") == 0;
+    const bool only_single = force && std::strcmp(force, "single") == 0;
     GemmPlan best;
     double best_score = -1.0;
-    // relative tensor-pipe efficiency of narrower MMA shapes (wider N reuses A better)
+    // one CTA per SM: block 128 x {256, 128, 64}; relative tensor-pipe
+    // efficiency of narrower MMA shapes (wider N reuses A more)
     const int cand[3] = {256, 128, 64};
     const double mma_eff[3] = {1.0, 0.93, 0.80};
+    const double mcov1 = static_cast<double>(m) / static_cast<double>(cdiv(m, kBlockM) * kBlockM);
     for (int i = 0; i < 3; ++i) {
         const int bn = cand[i];
         const int64_t tiles = cdiv(m, kBlockM) * cdiv(n, bn);
         const int64_t waves = cdiv(tiles, sm_count);
         const double fill = static_cast<double>(tiles) / static_cast<double>(waves * sm_count);
-        // wasted columns of a partial last N tile
         const double ncov = static_cast<double>(n) / static_cast<double>(cdiv(n, bn) * bn);
-        const double score = fill * ncov * mma_eff[i];
-        if (score > best_score + 1e-9) {
+        const double score = fill * ncov * mcov1 * mma_eff[i];
+        if (!only_pair && score > best_score + 1e-9) {
             best_score = score;
+            best.pair = false;
+            best.block_m = kBlockM;
             best.block_n = bn;
             best.tiles = static_cast<int>(tiles);
         }
     }
-    best.block_m = kBlockM;
+    // CTA pairs: 256 x 256 per pair, half the staged B bytes per SM
+    {
+        const int pairs = sm_count / 2;
+        const int64_t tiles = cdiv(m, 2 * kBlockM) * cdiv(n, kPairN);
+        const int64_t waves = cdiv(tiles, pairs);
+        const double fill = static_cast<double>(tiles) / static_cast<double>(waves * pairs);
+        const double ncov = static_cast<double>(n) / static_cast<double>(cdiv(n, kPairN) * kPairN);
+        const double mcov = static_cast<double>(m) / static_cast<double>(cdiv(m, 2 * kBlockM) * 2 * kBlockM);
+        const double score = fill * ncov * mcov * 1.10;
+        if (!only_single && (only_pair || score > best_score + 1e-9)) {
+            best_score = score;
+            best.pair = true;
+            best.block_m = 2 * kBlockM;
+            best.block_n = kPairN;
+            best.tiles = static_cast<int>(tiles);
+        }
+    }
     best.block_k = in_dtype == ST_F32 ? 32 : 64;
-    best.stages = best.block_n == 256 ? TileCfg<256>::kStages
-                                      : (best.block_n == 128 ? TileCfg<128>::kStages : TileCfg<64>::kStages);
-    best.ctas = best.tiles < sm_count ? best.tiles : sm_count;
+    if (best.pair) {
+        best.stages = PairCfg::kStages;
+        const int pairs = best.tiles < sm_count / 2 ? best.tiles : sm_count / 2;
+        best.ctas = 2 * pairs;
+    } else {
+        best.stages = best.block_n == 256 ? TileCfg<256>::kStages
+                                          : (best.block_n == 128 ? TileCfg<128>::kStages : TileCfg<64>::kStages);
+        best.ctas = best.tiles < sm_count ? best.tiles : sm_count;
+    }
     *plan = best;
     return ST_OK;
 }
@@ -448,7 +761,7 @@ int launch_gemm(const GemmArgs &g, int sm_count, int *dev_err, uint64_t timeout_
                     static_cast<uint64_t>(g.lda) * elem, bk, kBlockM));
     if (g.b_k_major) {
         ST_TRY(make_map(&mb, dt, g.b, static_cast<uint64_t>(g.k), static_cast<uint64_t>(g.n),
-                        static_cast<uint64_t>(g.ldb) * elem, bk, plan.block_n));
+                        static_cast<uint64_t>(g.ldb) * elem, bk, plan.pair ? kPairHalfN : plan.block_n));
     } else {
         ST_TRY(make_map(&mb, dt, g.b, static_cast<uint64_t>(g.n), static_cast<uint64_t>(g.k),
                         static_cast<uint64_t>(g.ldb) * elem, 64, bk));
@@ -468,6 +781,16 @@ int launch_gemm(const GemmArgs &g, int sm_count, int *dev_err, uint64_t timeout_
     kp.bias_dtype = g.bias_dtype;
     kp.err = dev_err;
     kp.timeout_ns = timeout_ns;
+    if (plan.pair) {
+        const int pairs = plan.ctas / 2;
+        if (g.ab_dtype == ST_F16)
+            return g.b_k_major ? launch_pair<0, false>(ma, mb, kp, pairs, stream)
+                               : launch_pair<0, true>(ma, mb, kp, pairs, stream);
+        if (g.ab_dtype == ST_BF16)
+            return g.b_k_major ? launch_pair<1, false>(ma, mb, kp, pairs, stream)
+                               : launch_pair<1, true>(ma, mb, kp, pairs, stream);
+        return launch_pair<2, false>(ma, mb, kp, pairs, stream);
+    }
     if (g.ab_dtype == ST_F16) {
         return g.b_k_major ? dispatch_bn<0, false>(plan.block_n, ma, mb, kp, plan.ctas, stream)
                            : dispatch_bn<0, true>(plan.block_n, ma, mb, kp, plan.ctas, stream);

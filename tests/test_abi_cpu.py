@@ -75,17 +75,28 @@ def test_tile_raster_rejects_bad_arguments():
                                       (N.ST_F16, 100, 70, 33), (N.ST_BF16, 4096, 4096, 4096)])
 def test_matmul_plan_is_sane(dt, m, n, k):
     p = st.matmul_plan(dt, m, n, k, 148)
-    assert p["block_m"] == 128 and p["block_n"] in (64, 128, 256)
+    assert (p["block_m"], p["block_n"]) in ((128, 64), (128, 128), (128, 256), (256, 256))
     assert p["block_k"] * (4 if dt == N.ST_F32 else 2) == 128
-    tiles = -(-m // 128) * -(-n // p["block_n"])
-    assert p["ctas"] == min(tiles, 148)
+    tiles = -(-m // p["block_m"]) * -(-n // p["block_n"])
+    if p["block_m"] == 256:  # CTA pairs: two CTAs per tile, at most 74 pairs
+        assert p["ctas"] == 2 * min(tiles, 74)
+    else:
+        assert p["ctas"] == min(tiles, 148)
     assert 2 <= p["stages"] <= 8
 
 
 def test_matmul_plan_headline_shapes():
-    assert st.matmul_plan(N.ST_F16, 8192, 8192, 8192)["block_n"] == 256
+    big = st.matmul_plan(N.ST_F16, 8192, 8192, 8192)
+    assert (big["block_m"], big["block_n"], big["ctas"]) == (256, 256, 148)  # CTA pairs
     # a small fp32 problem spreads over more SMs with narrower tiles
     assert st.matmul_plan(N.ST_F32, 1024, 1024, 1024)["ctas"] >= 64
+
+
+def test_kernel_family_override(monkeypatch):
+    monkeypatch.setenv("SPTILES_B200_GEMM_KERNEL", "single")
+    assert st.matmul_plan(N.ST_F16, 8192, 8192, 8192)["block_m"] == 128
+    monkeypatch.setenv("SPTILES_B200_GEMM_KERNEL", "pair")
+    assert st.matmul_plan(N.ST_F32, 100, 70, 33)["block_m"] == 256
 
 
 @pytest.mark.parametrize("total,count,align", [(8192, 8, 128), (8192, 3, 128), (100, 4, 4), (5, 8, 4),
