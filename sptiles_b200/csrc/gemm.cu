@@ -359,11 +359,28 @@ __global__ void __launch_bounds__(kThreads, 1)
 constexpr int kPairN = 256;      // N of one pair MMA
 constexpr int kPairHalfN = 128;  // columns of B each CTA stages
 
+#ifndef ST_PAIR_STAGES
+#define ST_PAIR_STAGES 6
+#endif
+#ifndef ST_L2_POLICY
+#define ST_L2_POLICY 1  // operand loads: 0 evict_normal, 1 evict_last
+#endif
+
+__device__ __forceinline__ uint64_t operand_l2_policy() {
+#if ST_L2_POLICY == 1
+    return l2_policy_evict_last();
+#else
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(p));
+    return p;
+#endif
+}
+
 struct PairCfg {
     static constexpr int kABytes = kBlockM * kRowBytes;
     static constexpr int kBBytes = kPairHalfN * kRowBytes;
     static constexpr int kStageBytes = kABytes + kBBytes;
-    static constexpr int kStages = 6;
+    static constexpr int kStages = ST_PAIR_STAGES;
     static constexpr int kTmemCols = 512;  // two 256-column accumulators
     static constexpr int kSmemBytes = kStages * kStageBytes + 256 + 1024;
 };
@@ -434,7 +451,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     if (warp == 0) {
         // ------------------------------------------------ TMA producer (both CTAs)
         if (lane == 0) {
-            const uint64_t pol = l2_policy_evict_last();
+            const uint64_t pol = operand_l2_policy();
             int s = 0;
             uint32_t ph = 0;
             int round = 0;  // passes over the ring completed

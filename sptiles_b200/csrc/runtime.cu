@@ -63,6 +63,11 @@ struct DeviceState {
     int *dev_err = nullptr;
     Workspace scratch;  // packed / repacked matmul operands
     Workspace stage;    // device copies of host-memory arguments
+    // host-memory calls: copies in and out run on their own streams so that
+    // both PCIe directions overlap the kernels
+    cudaStream_t copy_in = nullptr;
+    cudaStream_t copy_out = nullptr;
+    std::vector<cudaEvent_t> events;  // reusable ordering events
 };
 
 class DeviceGuard {
@@ -429,6 +434,155 @@ size_t staged_bytes(const st_tensor &t) {
     return (n + 255) & ~size_t(255);
 }
 
+// ------------------------------------------------------------ pipelined host calls
+// Event `i` of the device's pool (created on first use, reused afterwards).
+int pool_event(DeviceState *d, size_t i, cudaEvent_t *out) {
+    while (d->events.size() <= i) {
+        cudaEvent_t e;
+        ST_CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+        d->events.push_back(e);
+    }
+    *out = d->events[i];
+    return ST_OK;
+}
+
+int ensure_copy_streams(DeviceState *d) {
+    if (!d->copy_in) ST_CUDA_TRY(cudaStreamCreateWithFlags(&d->copy_in, cudaStreamNonBlocking));
+    if (!d->copy_out) ST_CUDA_TRY(cudaStreamCreateWithFlags(&d->copy_out, cudaStreamNonBlocking));
+    return ST_OK;
+}
+
+// `waiter` waits for everything issued so far on `signaller`.
+int stream_after(DeviceState *d, size_t &ev_i, cudaStream_t waiter, cudaStream_t signaller) {
+    cudaEvent_t e;
+    ST_TRY(pool_event(d, ev_i++, &e));
+    ST_CUDA_TRY(cudaEventRecord(e, signaller));
+    ST_CUDA_TRY(cudaStreamWaitEvent(waiter, e, 0));
+    return ST_OK;
+}
+
+bool host_rows_dense(const st_tensor &t) {  // unit column stride (rows may be padded)
+    if (t.rank == 1) return t.shape[0] <= 1 || t.strides[0] == 1;
+    return t.shape[1] <= 1 || t.strides[1] == 1;
+}
+
+// rows [r0, r1) of a rank-2 host tensor <-> a dense device block
+int copy_rows_in(cudaStream_t s, void *dst, const st_tensor &h, int64_t r0, int64_t r1) {
+    const size_t es = dtype_size(h.dtype);
+    const int64_t cols = h.shape[1];
+    if (r1 <= r0 || cols == 0) return ST_OK;
+    const int64_t hs0 = h.shape[0] > 1 ? h.strides[0] : cols;
+    const uint8_t *src = static_cast<const uint8_t *>(h.data) + static_cast<size_t>(r0 * hs0) * es;
+    ST_CUDA_TRY(cudaMemcpy2DAsync(dst, cols * es, src, hs0 * es, cols * es, r1 - r0, cudaMemcpyHostToDevice, s));
+    return ST_OK;
+}
+
+int copy_rows_out(cudaStream_t s, const st_tensor &h, const void *src, int64_t r0, int64_t r1) {
+    const size_t es = dtype_size(h.dtype);
+    const int64_t cols = h.shape[1];
+    if (r1 <= r0 || cols == 0) return ST_OK;
+    const int64_t hs0 = h.shape[0] > 1 ? h.strides[0] : cols;
+    uint8_t *dst = static_cast<uint8_t *>(h.data) + static_cast<size_t>(r0 * hs0) * es;
+    ST_CUDA_TRY(cudaMemcpy2DAsync(dst, hs0 * es, src, cols * es, cols * es, r1 - r0, cudaMemcpyDeviceToHost, s));
+    return ST_OK;
+}
+
+// C = A @ B (+ bias) on host tensors with 16-bit A and B:
+//   copy_in : B (and bias), then A in row chunks
+//   compute : chunk i's GEMM once its rows of A are in
+//   copy_out: chunk i's rows of C once its GEMM is done
+int matmul_host_pipelined(const ExecCtx &x, const st_tensor &a, const st_tensor &b, const st_tensor *bias,
+                          const st_tensor &c) {
+    DeviceState *d = x.dev;
+    ST_TRY(ensure_copy_streams(d));
+    const int64_t M = a.shape[0], K = a.shape[1], N = b.shape[1];
+    const size_t ein = dtype_size(a.dtype), eout = dtype_size(c.dtype);
+    const size_t a_bytes = static_cast<size_t>(M * K) * ein, b_bytes = static_cast<size_t>(K * N) * ein;
+    const size_t c_bytes = static_cast<size_t>(M * N) * eout;
+    const size_t bias_bytes = bias ? static_cast<size_t>(N) * dtype_size(bias->dtype) : 0;
+    auto up = [](size_t v) { return (v + 255) & ~size_t(255); };
+    void *base = nullptr;
+    ST_TRY(ws_acquire(d->stage, up(a_bytes) + up(b_bytes) + up(c_bytes) + up(bias_bytes), x.stream, &base));
+    uint8_t *da = static_cast<uint8_t *>(base);
+    uint8_t *db = da + up(a_bytes);
+    uint8_t *dc = db + up(b_bytes);
+    uint8_t *dbias = dc + up(c_bytes);
+    size_t ev = 0;
+    // the copies start after earlier work on the caller's stream (workspace reuse)
+    ST_TRY(stream_after(d, ev, d->copy_in, x.stream));
+    ST_TRY(stream_after(d, ev, d->copy_out, x.stream));
+    ST_TRY(copy_rows_in(d->copy_in, db, b, 0, K));
+    if (bias) ST_CUDA_TRY(cudaMemcpyAsync(dbias, bias->data, bias_bytes, cudaMemcpyHostToDevice, d->copy_in));
+    ST_TRY(stream_after(d, ev, x.stream, d->copy_in));
+    // ~16 MB of A per chunk, in whole 256-row tiles
+    int64_t rows = static_cast<int64_t>((size_t(16) << 20) / std::max<size_t>(1, static_cast<size_t>(K) * ein));
+    rows = std::max<int64_t>(256, (rows / 256) * 256);
+    st_tensor vb = b;
+    vb.data = db;
+    vb.strides[0] = N;
+    vb.strides[1] = 1;
+    st_tensor vbias;
+    if (bias) {
+        vbias = *bias;
+        vbias.data = dbias;
+        vbias.strides[0] = 1;
+    }
+    for (int64_t r0 = 0; r0 < M; r0 += rows) {
+        const int64_t r1 = std::min(M, r0 + rows);
+        uint8_t *da_i = da + static_cast<size_t>(r0 * K) * ein;
+        uint8_t *dc_i = dc + static_cast<size_t>(r0 * N) * eout;
+        ST_TRY(copy_rows_in(d->copy_in, da_i, a, r0, r1));
+        ST_TRY(stream_after(d, ev, x.stream, d->copy_in));
+        st_tensor va = a, vc = c;
+        va.data = da_i;
+        va.shape[0] = r1 - r0;
+        va.strides[0] = K;
+        va.strides[1] = 1;
+        vc.data = dc_i;
+        vc.shape[0] = r1 - r0;
+        vc.strides[0] = N;
+        vc.strides[1] = 1;
+        ST_TRY(matmul_device(x, va, vb, bias ? &vbias : nullptr, vc));
+        ST_TRY(stream_after(d, ev, d->copy_out, x.stream));
+        ST_TRY(copy_rows_out(d->copy_out, c, dc_i, r0, r1));
+    }
+    ST_TRY(stream_after(d, ev, x.stream, d->copy_out));
+    ST_TRY(ws_release(d->stage, x.stream));
+    return bounded_sync(d, x.stream, x.timeout_ms);
+}
+
+// C = A + B on dense host arrays, in element chunks over the three streams.
+int vector_add_host_pipelined(const ExecCtx &x, const st_tensor &a, const st_tensor &b, const st_tensor &c,
+                              int64_t n) {
+    DeviceState *d = x.dev;
+    ST_TRY(ensure_copy_streams(d));
+    const size_t bytes = static_cast<size_t>(n) * 4;
+    auto up = [](size_t v) { return (v + 255) & ~size_t(255); };
+    void *base = nullptr;
+    ST_TRY(ws_acquire(d->stage, 3 * up(bytes), x.stream, &base));
+    float *da = static_cast<float *>(base);
+    float *db = reinterpret_cast<float *>(static_cast<uint8_t *>(base) + up(bytes));
+    float *dc = reinterpret_cast<float *>(static_cast<uint8_t *>(base) + 2 * up(bytes));
+    const float *ha = static_cast<const float *>(a.data), *hb = static_cast<const float *>(b.data);
+    float *hc = static_cast<float *>(c.data);
+    size_t ev = 0;
+    ST_TRY(stream_after(d, ev, d->copy_in, x.stream));
+    ST_TRY(stream_after(d, ev, d->copy_out, x.stream));
+    const int64_t chunk = int64_t(4) << 20;  // 16 MB of each array per chunk
+    for (int64_t e0 = 0; e0 < n; e0 += chunk) {
+        const int64_t len = std::min(chunk, n - e0);
+        ST_CUDA_TRY(cudaMemcpyAsync(da + e0, ha + e0, len * 4, cudaMemcpyHostToDevice, d->copy_in));
+        ST_CUDA_TRY(cudaMemcpyAsync(db + e0, hb + e0, len * 4, cudaMemcpyHostToDevice, d->copy_in));
+        ST_TRY(stream_after(d, ev, x.stream, d->copy_in));
+        ST_TRY(launch_vector_add_1d(da + e0, 1, db + e0, 1, dc + e0, 1, len, d->sm_count, x.stream));
+        ST_TRY(stream_after(d, ev, d->copy_out, x.stream));
+        ST_CUDA_TRY(cudaMemcpyAsync(hc + e0, dc + e0, len * 4, cudaMemcpyDeviceToHost, d->copy_out));
+    }
+    ST_TRY(stream_after(d, ev, x.stream, d->copy_out));
+    ST_TRY(ws_release(d->stage, x.stream));
+    return bounded_sync(d, x.stream, x.timeout_ms);
+}
+
 // ------------------------------------------------------------ entry registry
 enum class Kind { VectorAdd1D, VectorAdd2D, Matmul };
 
@@ -645,8 +799,13 @@ int st_shutdown(st_ctx *ctx) {
     for (auto &d : ctx->devs) {
         DeviceGuard guard(d.ordinal);
         if (d.stream) cudaStreamSynchronize(d.stream);
+        if (d.copy_in) cudaStreamSynchronize(d.copy_in);
+        if (d.copy_out) cudaStreamSynchronize(d.copy_out);
         ws_free(d.scratch);
         ws_free(d.stage);
+        for (cudaEvent_t e : d.events) cudaEventDestroy(e);
+        if (d.copy_in) cudaStreamDestroy(d.copy_in);
+        if (d.copy_out) cudaStreamDestroy(d.copy_out);
         if (d.dev_err) cudaFree(d.dev_err);
         if (d.stream) cudaStreamDestroy(d.stream);
     }
@@ -799,6 +958,17 @@ int st_vector_add_host(st_ctx *ctx, const st_tensor *a, const st_tensor *b, cons
     ST_TRY(resolve_exec(ctx, exec, &x));
     ST_TRY(check_vector_add(a, b, c));
     DeviceGuard guard(x.dev->ordinal);
+    {
+        // dense arrays of the same layout: one flat range, pipelined
+        bool flat = true;
+        int64_t n = 1;
+        for (const st_tensor *t : {a, b, c}) {
+            if (t->rank == 1) flat &= t->shape[0] <= 1 || t->strides[0] == 1;
+            else flat &= (t->shape[1] <= 1 || t->strides[1] == 1) && (t->shape[0] <= 1 || t->strides[0] == t->shape[1]);
+        }
+        for (int i = 0; i < c->rank; ++i) n *= c->shape[i];
+        if (flat && n > 0) return vector_add_host_pipelined(x, *a, *b, *c, n);
+    }
     void *base = nullptr;
     ST_TRY(ws_acquire(x.dev->stage, staged_bytes(*a) + staged_bytes(*b) + staged_bytes(*c), x.stream, &base));
     uint8_t *cursor = static_cast<uint8_t *>(base);
@@ -826,6 +996,11 @@ int st_matmul_host(st_ctx *ctx, const st_tensor *a, const st_tensor *b, const st
     ST_TRY(resolve_exec(ctx, exec, &x));
     ST_TRY(check_matmul(a, b, bias, c));
     DeviceGuard guard(x.dev->ordinal);
+    // 16-bit operands with unit column strides: chunked and overlapped (the
+    // fp32 path packs B once per call, so it stays unchunked)
+    if (a->dtype != ST_F32 && a->shape[0] > 0 && b->shape[1] > 0 && a->shape[1] > 0 && host_rows_dense(*a) &&
+        host_rows_dense(*b) && host_rows_dense(*c))
+        return matmul_host_pipelined(x, *a, *b, bias, *c);
     size_t need = staged_bytes(*a) + staged_bytes(*b) + staged_bytes(*c) + (bias ? staged_bytes(*bias) : 0);
     void *base = nullptr;
     ST_TRY(ws_acquire(x.dev->stage, need, x.stream, &base));

@@ -286,3 +286,26 @@ def test_kernel_families_random_with_bias(monkeypatch, family, dtype):
     bias = normal((n,), 1.0, 72, torch.float32)
     C = st.matmul(A, B, bias, out_dtype=torch.float32)
     assert rel_err(C.cpu().numpy(), oracle_mm(A, B, bias)) <= TOL[dtype]
+
+
+# ------------------------------------------------------------ host-memory calls
+@pytest.mark.parametrize("pinned", [True, False])
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16], ids=["f16", "bf16"])
+def test_host_tensors_chunked_pipeline(pinned, dtype):
+    """16-bit host operands go through the chunked copy-in / GEMM / copy-out pipeline."""
+    m, n, k = 2600, 1100, 4104  # ~16 MB row chunks of A, whole 256-row tiles -> 1792 + 808 rows
+    A, B = normal((m, k), 0.3, 90, dtype).cpu(), normal((k, n), 0.3, 91, dtype).cpu()
+    bias = normal((n,), 1.0, 92, torch.float32).cpu()
+    if pinned:
+        A, B, bias = A.pin_memory(), B.pin_memory(), bias.pin_memory()
+    C = st.matmul(A, B, bias, out_dtype=torch.float32)
+    assert C.device.type == "cpu"
+    Cd = st.matmul(A.to(DEV), B.to(DEV), bias.to(DEV), out_dtype=torch.float32)
+    assert rel_err(C.numpy(), Cd.cpu().numpy()) <= 1e-6
+    for r0, r1 in ((0, 8), (1784, 1800), (m - 8, m)):  # both chunks and the seam
+        want = oracle_mm(A, B, bias, rows=(r0, r1))
+        assert rel_err(C[r0:r1].numpy(), want) <= TOL[dtype]
+    # padded host output rows
+    out = torch.full((m, n + 3), 7.0)
+    st.matmul(A, B, bias, out=out[:, :n])
+    assert torch.equal(out[:, :n], C) and torch.all(out[:, n:] == 7.0)

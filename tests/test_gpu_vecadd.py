@@ -164,3 +164,18 @@ def test_descriptor_reaching_past_buffer_is_rejected():
     A = torch.zeros(100, device=DEV)
     with pytest.raises(ValueError, match="past its buffer"):
         _launch("vector_add", (1, 1, 1), [A, 200, 1, A, 100, 1, A, 100, 1])
+
+
+@pytest.mark.parametrize("pinned", [True, False])
+def test_host_arrays_chunked_pipeline(pinned):
+    n = 10_000_003  # three 4M-element chunks, ragged tail
+    a, b = uniform(n, 50), uniform(n, 51)
+    A, B = torch.from_numpy(a), torch.from_numpy(b)
+    if pinned:
+        A, B = A.pin_memory(), B.pin_memory()
+    C = st.vector_add(A, B)
+    assert C.device.type == "cpu"
+    assert C.numpy().tobytes() == oracle_add(a, b).tobytes()
+    # 2D host arrays flatten to the same pipeline
+    C2 = st.vector_add(A[: 4000 * 2500].view(4000, 2500), B[: 4000 * 2500].view(4000, 2500))
+    assert C2.numpy().tobytes() == oracle_add(a[: 10_000_000], b[: 10_000_000]).reshape(4000, 2500).tobytes()
