@@ -63,6 +63,10 @@ def parse_args():
     p.add_argument("--no-secondary", action="store_true", help="skip the vector_add measurement of the default run")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--timing", choices=["auto", "graph", "eager"], default="auto",
+                   help="graph: replay the K timed steps from one CUDA graph (host launch overhead out of the "
+                        "timed region); eager: launch every step from the host; auto: graph for the "
+                        "launch-bound vector_add workloads, eager for the matmuls")
     return p.parse_args()
 
 
@@ -181,26 +185,59 @@ def flops_of(wl, rows):
 
 
 # ------------------------------------------------------------------ our arm
-def time_steps(fn, steps, warmup, stream, dist_on):
-    """Per-step device time (ms) of `fn` over `steps` calls after `warmup` calls."""
+def time_steps(fn, steps, warmup, stream, dist_on, graph=True):
+    """Device time (ms) of `steps` calls of `fn` after `warmup` calls.
+
+    With ``graph`` the timed calls are captured once into a CUDA graph and
+    the timed region is one replay of it: every step is still one full call
+    of the hot path, but the host's per-call launch overhead leaves the
+    timed region (what a launch-bound inner loop does in production).
+    Returns (ms, launches issued by the library for the timed steps).
+    """
     import torch
     import torch.distributed as dist
+    import sptiles_b200 as st
     for _ in range(warmup):
         fn(-1)
     torch.cuda.synchronize()
+    g = None
+    if graph:
+        g = torch.cuda.CUDAGraph()
+        before = st.kernel_launches()
+        with torch.cuda.graph(g):
+            for i in range(steps):
+                fn(i)
+        launches = st.kernel_launches() - before
+        g.replay()  # upload the graph; untimed
+        torch.cuda.synchronize()
     if dist_on:
         dist.barrier()
     torch.cuda.synchronize()
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
+    stream = torch.cuda.current_stream()
+    if g is None:
+        before = st.kernel_launches()
     start.record(stream)
-    for i in range(steps):
-        fn(i)
+    if g is not None:
+        g.replay()
+    else:
+        for i in range(steps):
+            fn(i)
     end.record(stream)
     torch.cuda.synchronize()
+    if g is None:
+        launches = st.kernel_launches() - before
     if dist_on:
         dist.barrier()
-    return start.elapsed_time(end)
+    del g
+    return start.elapsed_time(end), launches
+
+
+def use_graph(args, wl):
+    if args.timing == "auto":
+        return wl["kind"] == "vector_add"
+    return args.timing == "graph"
 
 
 def max_over_ranks(x, dist_on):
@@ -240,10 +277,8 @@ def run_matmul(wl, args, rank, world, local, dist_on, peaks):
         if rows:
             st.matmul(a, b, bias, out=c)
 
-    launches0 = st.kernel_launches()
     with ClockSampler(local) as clk:
-        ms = time_steps(step, args.steps, args.warmup, stream, dist_on)
-    launches = st.kernel_launches() - launches0 - args.warmup * (1 if rows else 0) * per_call_launches(wl)
+        ms, launches = time_steps(step, args.steps, args.warmup, stream, dist_on, graph=use_graph(args, wl))
     ms_max = max_over_ranks(ms, dist_on)
     total_flops = sum_over_ranks(flops_of(wl, rows), dist_on)
     value = total_flops * args.steps / (ms_max / 1e3) / 1e12
@@ -266,10 +301,6 @@ def run_matmul(wl, args, rank, world, local, dist_on, peaks):
     if not args.no_e2e:
         out["e2e"] = e2e_matmul(wl, args, a, b, bias, out_dt, rows, dist_on)
     return out
-
-
-def per_call_launches(wl):
-    return 3 if wl["dtype"] == "f32" else 1
 
 
 def e2e_matmul(wl, args, a, b, bias, out_dt, rows, dist_on):
@@ -332,10 +363,8 @@ def run_vector_add(wl, args, rank, world, local, dist_on, peaks):
         a, b, c = bufs[i % sets]
         st.vector_add(a, b, out=c)
 
-    launches0 = st.kernel_launches()
     with ClockSampler(local) as clk:
-        ms = time_steps(step, args.steps, args.warmup, stream, dist_on)
-    launches = st.kernel_launches() - launches0 - args.warmup
+        ms, launches = time_steps(step, args.steps, args.warmup, stream, dist_on, graph=use_graph(args, wl))
     ms_max = max_over_ranks(ms, dist_on)
     total_bytes = sum_over_ranks(bytes_per_step, dist_on)
     value = total_bytes * args.steps / (ms_max / 1e3) / 1e9
@@ -489,7 +518,15 @@ def run_reference(args, rank, world):
     return 0
 
 
-def config_of(name, wl, n_gpus):
+def config_of(name, wl, n_gpus, timing="auto"):
+    graph = (wl["kind"] == "vector_add") if timing == "auto" else timing == "graph"
+    how = "one CUDA-graph replay of the K steps" if graph else "K host launches"
+    cfg = _config_of(name, wl, n_gpus)
+    cfg["timed_region"] = how
+    return cfg
+
+
+def _config_of(name, wl, n_gpus):
     if wl["kind"] == "matmul":
         return {"workload": name, "M": wl["m"], "N": wl["n"], "K": wl["k"], "in_dtype": wl["dtype"],
                 "out_dtype": wl["out"], "bias": wl["bias"], "parallelism": f"M-row shards x{n_gpus}",
@@ -530,7 +567,7 @@ def main():
                          "steps": sub_args.steps, "warmup": sub_args.warmup,
                          "ms_per_step": round(sub["ms_per_step"], 5), "roofline": sub["roofline"],
                          "e2e": sub.get("e2e"), "gpu_launches": sub["gpu_launches"], "clocks": sub["clocks"],
-                         "config": config_of("vector_add_2d", vw, world)}
+                         "config": config_of("vector_add_2d", vw, world, args.timing)}
         cpu = None
         if rank == 0 and world == 1 and not args.no_cpu_baseline:
             cpu = cpu_baseline(wl)
@@ -541,7 +578,7 @@ def main():
                 "warmup": args.warmup, "ms_per_step": round(res["ms_per_step"], 5), "higher_is_better": True,
                 "scaling": "strong", "vs_baseline": None, "dtype": wl.get("dtype", "f32"),
                 "data": "synthetic (seeded; shapes and distributions of the configuration)",
-                "config": config_of(args.workload, wl, world), "roofline": res["roofline"],
+                "config": config_of(args.workload, wl, world, args.timing), "roofline": res["roofline"],
                 "cpu_baseline": cpu, "e2e": res.get("e2e"), "gpu_launches": res["gpu_launches"],
                 "clocks": res["clocks"],
             }

@@ -108,8 +108,21 @@ int get_dev(st_ctx *ctx, int device, DeviceState **out) {
     return ST_OK;
 }
 
-// Grow `ws` to at least `need` bytes for use on `stream`.
+bool capturing(cudaStream_t stream) {
+    cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
+    return cudaStreamIsCapturing(stream, &st) == cudaSuccess && st != cudaStreamCaptureStatusNone;
+}
+
+// Grow `ws` to at least `need` bytes for use on `stream`.  While `stream` is
+// being captured into a CUDA graph the buffer must already be large enough
+// (a warm-up call sizes it) and stream order alone sequences its users.
 int ws_acquire(Workspace &ws, size_t need, cudaStream_t stream, void **out) {
+    if (capturing(stream)) {
+        if (need > ws.bytes)
+            return fail(ST_ERR_UNSUPPORTED, "the workspace must be sized by an uncaptured call before graph capture");
+        *out = ws.ptr;
+        return ST_OK;
+    }
     if (ws.ready == nullptr) ST_CUDA_TRY(cudaEventCreateWithFlags(&ws.ready, cudaEventDisableTiming));
     // a previous user on another stream must be done with the buffer
     ST_CUDA_TRY(cudaStreamWaitEvent(stream, ws.ready, 0));
@@ -129,6 +142,7 @@ int ws_acquire(Workspace &ws, size_t need, cudaStream_t stream, void **out) {
 }
 
 int ws_release(Workspace &ws, cudaStream_t stream) {
+    if (capturing(stream)) return ST_OK;
     ST_CUDA_TRY(cudaEventRecord(ws.ready, stream));
     return ST_OK;
 }

@@ -309,3 +309,21 @@ def test_host_tensors_chunked_pipeline(pinned, dtype):
     out = torch.full((m, n + 3), 7.0)
     st.matmul(A, B, bias, out=out[:, :n])
     assert torch.equal(out[:, :n], C) and torch.all(out[:, n:] == 7.0)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16], ids=["f32", "f16"])
+def test_calls_replay_from_a_cuda_graph(dtype):
+    """Device-tensor calls issued inside torch.cuda.graph replay correctly."""
+    m, n, k = 512, 384, 320
+    A, B = kat(m, n, k, dtype)
+    C = torch.zeros((m, n), device=DEV)
+    st.matmul(A, B, out=C.to(dtype) if dtype != torch.float32 else C)  # warm-up sizes any workspace
+    torch.cuda.synchronize()
+    out = torch.zeros((m, n), device=DEV)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        st.matmul(A, B, out=out)
+    out.fill_(-1.0)
+    g.replay()
+    torch.cuda.synchronize()
+    assert out.cpu().numpy().tobytes() == oracle.matmul_kat_expected(m, n, k).tobytes()
