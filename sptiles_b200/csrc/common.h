@@ -92,6 +92,11 @@ struct GemmArgs {
     int64_t m, n, k;
 };
 int launch_gemm(const GemmArgs &args, int sm_count, int *dev_err, uint64_t timeout_ns, cudaStream_t stream);
+// fp32 A and B used in place (TMA-addressable): the split into tf32 hi/lo
+// happens in shared memory inside the kernel (args.ab_dtype must be ST_F32,
+// args.k the true K).
+int plan_gemm_x3(int64_t m, int64_t n, bool b_n_contiguous, int sm_count, GemmPlan *plan);
+int launch_gemm_3xtf32(const GemmArgs &args, int sm_count, int *dev_err, uint64_t timeout_ns, cudaStream_t stream);
 
 // 3xTF32 operand preparation.  x = hi + lo with hi, lo tf32-exact.
 //   A [M, K] (strides sa0, sa1) -> Ap [M, 3*kp] = [hi | hi | lo], kp = round_up(K, 32)

@@ -56,7 +56,13 @@ constexpr int kBlockM = 128;
 constexpr int kRowBytes = 128;  // K bytes per stage row = one 128-byte swizzle span
 constexpr int kThreads = 192;   // 6 warps
 constexpr int kEpilogueWarps = 4;
-constexpr int kGroupM = 8;
+#ifndef ST_GROUP_M
+#define ST_GROUP_M 8
+#endif
+#ifndef ST_C_POLICY
+#define ST_C_POLICY 0  // C stores: 0 default, 1 L2 evict_first
+#endif
+constexpr int kGroupM = ST_GROUP_M;
 
 template <int BN>
 struct TileCfg {
@@ -102,9 +108,18 @@ __device__ __forceinline__ void store_row_chunk(const KParams &p, int row, int c
     if (p.c_dtype == ST_F32) {
         float *dst = static_cast<float *>(p.c) + off;
         if (cnt == 32 && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
+#if ST_C_POLICY == 1
+            const uint64_t pol = l2_policy_evict_first();
+#pragma unroll
+            for (int j = 0; j < 32; j += 4)
+                asm volatile("st.global.L2::cache_hint.v4.f32 [%0], {%1, %2, %3, %4}, %5;" ::"l"(dst + j),
+                             "f"(v[j]), "f"(v[j + 1]), "f"(v[j + 2]), "f"(v[j + 3]), "l"(pol)
+                             : "memory");
+#else
 #pragma unroll
             for (int j = 0; j < 32; j += 4)
                 *reinterpret_cast<float4 *>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+#endif
         } else {
 #pragma unroll
             for (int j = 0; j < 32; ++j)
@@ -594,6 +609,335 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     }
 }
 
+// ---------------------------------------------------------------- fp32 via 3xTF32, split in shared memory
+// fp32 A and B come in by TMA untouched; a converter warpgroup splits every
+// staged element x into tf32 hi = tf32(x) (written back in place) and
+// lo = tf32(x - hi) (written to a twin buffer with the same swizzled
+// layout), and the MMA warp issues hi*hi, hi*lo and lo*hi per K step of 8.
+// The split is elementwise, so the 128-byte swizzle of the staged tiles
+// needs no special handling; a proxy fence hands the converted bytes to the
+// tensor core.  Compared with packing the operands in global memory first,
+// HBM/L2 traffic drops from 3x to 1x of A and B and two launches disappear.
+constexpr int kX3SplitWarps = 8;
+constexpr int kX3SplitThreads = 32 * kX3SplitWarps;
+constexpr int kX3Threads = 192 + kX3SplitThreads;  // warps: 0 TMA, 1 MMA, 2-5 epilogue, 6.. split
+
+template <int BN, bool B_MN>
+struct X3Cfg {
+    static constexpr int kABytes = kBlockM * kRowBytes;  // 128 rows x 32 fp32
+    static constexpr int kBBytes = BN * kRowBytes;       // BN x 32 fp32
+    // per stage: A (hi in place), A lo, B hi, B lo, and for an N-contiguous B
+    // the raw tile (transposed into B hi / B lo by the split warps)
+    static constexpr int kStageBytes = 2 * kABytes + 2 * kBBytes + (B_MN ? kBBytes : 0);
+    static constexpr int kStages = (232448 - 1280) / kStageBytes > 4 ? 4 : (232448 - 1280) / kStageBytes;
+    static constexpr int kTmemCols = 2 * BN;
+    static constexpr int kSmemBytes = kStages * kStageBytes + 256 + 1024;
+    static_assert(kStages >= 3, "too few pipeline stages");
+};
+
+__device__ __forceinline__ uint32_t tf32_bits(float x) {
+    uint32_t u = __float_as_uint(x);
+    if ((u & 0x7f800000u) == 0x7f800000u) return u;
+    u += 0x0fffu + ((u >> 13) & 1u);
+    return u & 0xffffe000u;
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+template <bool B_MN, int BN>
+__global__ void __launch_bounds__(kX3Threads, 1)
+    gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                       const KParams p) {
+    using Cfg = X3Cfg<BN, B_MN>;
+    constexpr int kBK = 32;          // fp32 elements per stage row (128 bytes)
+    constexpr int kMmaK = 8;         // K per tcgen05.mma kind::tf32
+    constexpr int kKSteps = kBK / kMmaK;
+    // tf32 operands are always handed to the MMA K-major: an N-contiguous
+    // tf32 B read by the tensor core comes back as zeros on sm_100a, so an
+    // N-contiguous B is transposed by the split warps
+    constexpr uint32_t kIdesc = mma_idesc(2, false, false, kBlockM, BN);
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + Cfg::kStages * Cfg::kStageBytes);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 3 * Cfg::kStages + 5);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t bar0 = smem_addr(bars);
+    auto full_bar = [&](int s) { return bar0 + 8u * s; };
+    auto split_bar = [&](int s) { return bar0 + 8u * (Cfg::kStages + s); };
+    auto empty_bar = [&](int s) { return bar0 + 8u * (2 * Cfg::kStages + s); };
+    auto tfull_bar = [&](int a) { return bar0 + 8u * (3 * Cfg::kStages + a); };
+    auto tempty_bar = [&](int a) { return bar0 + 8u * (3 * Cfg::kStages + 2 + a); };
+    const uint32_t drain_bar = bar0 + 8u * (3 * Cfg::kStages + 4);
+    // stage s: [A | A lo | B | B lo]
+    auto a_of = [&](int s) { return smem + s * Cfg::kStageBytes; };
+    auto alo_of = [&](int s) { return smem + s * Cfg::kStageBytes + Cfg::kABytes; };
+    auto b_of = [&](int s) { return smem + s * Cfg::kStageBytes + 2 * Cfg::kABytes; };
+    auto blo_of = [&](int s) { return smem + s * Cfg::kStageBytes + 2 * Cfg::kABytes + Cfg::kBBytes; };
+    auto braw_of = [&](int s) { return smem + s * Cfg::kStageBytes + 2 * Cfg::kABytes + 2 * Cfg::kBBytes; };
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < Cfg::kStages; ++s) {
+            mbar_init(full_bar(s), 1);
+            mbar_init(split_bar(s), kX3SplitWarps);
+            mbar_init(empty_bar(s), 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(tfull_bar(a), 1);
+            mbar_init(tempty_bar(a), kEpilogueWarps);
+        }
+        mbar_init(drain_bar, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_map(&tmap_a);
+        tma_prefetch_map(&tmap_b);
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_addr(tmem_slot), Cfg::kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before_sync();
+    __syncthreads();
+    tc_fence_after_sync();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ------------------------------------------------ TMA producer
+        if (lane == 0) {
+            const uint64_t pol = l2_policy_evict_last();
+            int s = 0;
+            uint32_t ph = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; ok && t < p.total_tiles; t += gridDim.x) {
+                int64_t tm, tn;
+                tile_raster(p.num_m_tiles, p.num_n_tiles, kGroupM, t, tm, tn);
+                const int m0 = static_cast<int>(tm) * kBlockM;
+                const int n0 = static_cast<int>(tn) * BN;
+                for (int kb = 0; kb < p.num_k_blocks; ++kb) {
+                    if (!mbar_wait(empty_bar(s), ph ^ 1u, abort_flag, p.timeout_ns)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(full_bar(s), Cfg::kABytes + Cfg::kBBytes);
+                    tma_load_2d(smem_addr(a_of(s)), &tmap_a, full_bar(s), kb * kBK, m0, pol);
+                    if constexpr (B_MN) {
+                        // raw N-contiguous chunks of 32 columns x 32 K rows
+                        const uint32_t sraw = smem_addr(braw_of(s));
+#pragma unroll
+                        for (int j = 0; j < BN / 32; ++j)
+                            tma_load_2d(sraw + j * (kBK * 128), &tmap_b, full_bar(s), n0 + 32 * j, kb * kBK, pol);
+                    } else {
+                        tma_load_2d(smem_addr(b_of(s)), &tmap_b, full_bar(s), kb * kBK, n0, pol);
+                    }
+                    if (++s == Cfg::kStages) {
+                        s = 0;
+                        ph ^= 1u;
+                    }
+                }
+            }
+            if (!ok) {
+                *abort_flag = 1;
+                atomicExch(p.err, kDevAbortGemmProducer);
+            }
+        }
+    } else if (warp >= 6) {
+        // ------------------------------------------------ split warps: x -> (hi, lo)
+        // Each thread first issues all its shared-memory loads of the stage,
+        // then converts, then stores, so the loads overlap.
+        const int tid = threadIdx.x - 6 * 32;
+        constexpr int kAVec = Cfg::kABytes / 16 / kX3SplitThreads;  // float4 of A per thread
+        constexpr int kBVec = Cfg::kBBytes / 16 / kX3SplitThreads;  // K-groups of B per thread
+        static_assert(kAVec * 16 * kX3SplitThreads == Cfg::kABytes, "A split must divide evenly");
+        static_assert(kBVec * 16 * kX3SplitThreads == Cfg::kBBytes, "B split must divide evenly");
+        int s = 0;
+        uint32_t ph = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; ok && t < p.total_tiles; t += gridDim.x) {
+            for (int kb = 0; kb < p.num_k_blocks; ++kb) {
+                const bool ready = mbar_wait(full_bar(s), ph, abort_flag, p.timeout_ns);
+                if (!__all_sync(0xffffffffu, ready)) {
+                    ok = false;
+                    break;
+                }
+                float4 *a = reinterpret_cast<float4 *>(a_of(s));
+                float4 *alo = reinterpret_cast<float4 *>(alo_of(s));
+                float4 xa[kAVec];
+#pragma unroll
+                for (int q = 0; q < kAVec; ++q) xa[q] = a[tid + q * kX3SplitThreads];
+                float xb[kBVec][4];
+                if constexpr (B_MN) {
+                    // raw element (n, k) sits in 32-column chunk n/32, K row k, 16-byte
+                    // group (n%32)/4 swizzled with k%8
+                    const uint8_t *raw = braw_of(s);
+#pragma unroll
+                    for (int q = 0; q < kBVec; ++q) {
+                        const int idx = tid + q * kX3SplitThreads;
+                        const int n = idx % BN, kq = idx / BN, nl = n & 31;
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            const int k = kq * 4 + i;
+                            xb[q][i] = *reinterpret_cast<const float *>(
+                                raw + (n >> 5) * (kBK * 128) + k * 128 + (((nl >> 2) ^ (k & 7)) << 4) + ((nl & 3) << 2));
+                        }
+                    }
+                } else {
+                    const float4 *b = reinterpret_cast<const float4 *>(b_of(s));
+#pragma unroll
+                    for (int q = 0; q < kBVec; ++q) {
+                        const float4 v = b[tid + q * kX3SplitThreads];
+                        xb[q][0] = v.x;
+                        xb[q][1] = v.y;
+                        xb[q][2] = v.z;
+                        xb[q][3] = v.w;
+                    }
+                }
+#pragma unroll
+                for (int q = 0; q < kAVec; ++q) {
+                    float4 h, l;
+                    h.x = __uint_as_float(tf32_bits(xa[q].x));
+                    h.y = __uint_as_float(tf32_bits(xa[q].y));
+                    h.z = __uint_as_float(tf32_bits(xa[q].z));
+                    h.w = __uint_as_float(tf32_bits(xa[q].w));
+                    l.x = __uint_as_float(tf32_bits(xa[q].x - h.x));
+                    l.y = __uint_as_float(tf32_bits(xa[q].y - h.y));
+                    l.z = __uint_as_float(tf32_bits(xa[q].z - h.z));
+                    l.w = __uint_as_float(tf32_bits(xa[q].w - h.w));
+                    a[tid + q * kX3SplitThreads] = h;
+                    alo[tid + q * kX3SplitThreads] = l;
+                }
+#pragma unroll
+                for (int q = 0; q < kBVec; ++q) {
+                    float4 h, l;
+                    h.x = __uint_as_float(tf32_bits(xb[q][0]));
+                    h.y = __uint_as_float(tf32_bits(xb[q][1]));
+                    h.z = __uint_as_float(tf32_bits(xb[q][2]));
+                    h.w = __uint_as_float(tf32_bits(xb[q][3]));
+                    l.x = __uint_as_float(tf32_bits(xb[q][0] - h.x));
+                    l.y = __uint_as_float(tf32_bits(xb[q][1] - h.y));
+                    l.z = __uint_as_float(tf32_bits(xb[q][2] - h.z));
+                    l.w = __uint_as_float(tf32_bits(xb[q][3] - h.w));
+                    int off;
+                    if constexpr (B_MN) {
+                        // K-major home of (n, 4 kq .. 4 kq + 3): row n, 16-byte group kq ^ (n % 8)
+                        const int idx = tid + q * kX3SplitThreads;
+                        const int n = idx % BN, kq = idx / BN;
+                        off = n * 128 + ((kq ^ (n & 7)) << 4);
+                    } else {
+                        off = (tid + q * kX3SplitThreads) * 16;
+                    }
+                    *reinterpret_cast<float4 *>(b_of(s) + off) = h;
+                    *reinterpret_cast<float4 *>(blo_of(s) + off) = l;
+                }
+                fence_proxy_async_smem();  // generic-proxy writes -> tensor-core reads
+                __syncwarp();
+                if (lane == 0) mbar_arrive(split_bar(s));
+                if (++s == Cfg::kStages) {
+                    s = 0;
+                    ph ^= 1u;
+                }
+            }
+        }
+        if (!ok) *abort_flag = 1;
+    } else if (warp == 1) {
+        // ------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            int s = 0;
+            uint32_t ph = 0;
+            int iter = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; ok && t < p.total_tiles; t += gridDim.x, ++iter) {
+                const int acc = iter & 1;
+                const uint32_t acc_ph = static_cast<uint32_t>(iter >> 1) & 1u;
+                if (!mbar_wait(tempty_bar(acc), acc_ph ^ 1u, abort_flag, p.timeout_ns)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after_sync();
+                const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+                for (int kb = 0; kb < p.num_k_blocks; ++kb) {
+                    if (!mbar_wait(split_bar(s), ph, abort_flag, p.timeout_ns)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after_sync();
+                    const uint32_t sa = smem_addr(a_of(s)), salo = smem_addr(alo_of(s));
+                    const uint32_t sb = smem_addr(b_of(s)), sblo = smem_addr(blo_of(s));
+#pragma unroll
+                    for (int ks = 0; ks < kKSteps; ++ks) {
+                        const uint64_t ahi = smem_desc_sw128(sa + ks * 32, 16, 1024);
+                        const uint64_t alo = smem_desc_sw128(salo + ks * 32, 16, 1024);
+                        const uint64_t bhi = smem_desc_sw128(sb + ks * 32, 16, 1024);
+                        const uint64_t blo = smem_desc_sw128(sblo + ks * 32, 16, 1024);
+                        // small terms first, then the leading product
+                        tc_mma<true>(d_tmem, alo, bhi, kIdesc, (kb | ks) != 0 ? 1u : 0u);
+                        tc_mma<true>(d_tmem, ahi, blo, kIdesc, 1u);
+                        tc_mma<true>(d_tmem, ahi, bhi, kIdesc, 1u);
+                    }
+                    tc_commit(empty_bar(s));
+                    if (++s == Cfg::kStages) {
+                        s = 0;
+                        ph ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                tc_commit(tfull_bar(acc));
+            }
+            if (!ok) {
+                *abort_flag = 1;
+                atomicExch(p.err, kDevAbortGemmMma);
+            }
+            tc_commit(drain_bar);
+            (void)mbar_wait(drain_bar, 0, abort_flag, p.timeout_ns);
+        }
+    } else {
+        // ------------------------------------------------ epilogue (warps 2..5)
+        const int g = warp & 3;
+        int iter = 0;
+        for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x, ++iter) {
+            const int acc = iter & 1;
+            const uint32_t acc_ph = static_cast<uint32_t>(iter >> 1) & 1u;
+            int64_t tm, tn;
+            tile_raster(p.num_m_tiles, p.num_n_tiles, kGroupM, t, tm, tn);
+            const int m0 = static_cast<int>(tm) * kBlockM;
+            const int n0 = static_cast<int>(tn) * BN;
+            const bool ready = mbar_wait(tfull_bar(acc), acc_ph, abort_flag, p.timeout_ns);
+            if (!__all_sync(0xffffffffu, ready)) {
+                *abort_flag = 1;
+                if (lane == 0) atomicExch(p.err, kDevAbortGemmEpilogue);
+                break;
+            }
+            tc_fence_after_sync();
+            const int row = m0 + g * 32 + lane;
+            const uint32_t t_row = tmem_base + (static_cast<uint32_t>(g * 32) << 16) + static_cast<uint32_t>(acc * BN);
+#pragma unroll 1
+            for (int c = 0; c < BN / 32; ++c) {
+                uint32_t r[32];
+                tmem_load_32(t_row + c * 32, r);
+                tmem_load_wait();
+                const int col0 = n0 + c * 32;
+                if (row < p.m && col0 < p.n) store_row_chunk(p, row, col0, r);
+            }
+            tc_fence_before_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(tempty_bar(acc));
+        }
+    }
+
+    __syncthreads();
+    if (warp == 1) {
+        __syncwarp();
+        tc_fence_after_sync();
+        tmem_dealloc(tmem_base, Cfg::kTmemCols);
+    }
+}
+
 // ---------------------------------------------------------------- host side
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -694,7 +1038,94 @@ int launch_pair(const CUtensorMap &ma, const CUtensorMap &mb, const KParams &kp,
     return e == cudaSuccess ? ST_OK : cuda_fail(cudaGetLastError(), "gemm_tc_pair_kernel launch");
 }
 
+template <bool B_MN, int BN>
+int launch_x3_instance(const CUtensorMap &ma, const CUtensorMap &mb, const KParams &kp, int ctas,
+                       cudaStream_t stream) {
+    using Cfg = X3Cfg<BN, B_MN>;
+    auto kern = gemm_tf32x3_kernel<B_MN, BN>;
+    static uint64_t attr_set = 0;
+    int dev = 0;
+    ST_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64 || !(attr_set & (1ull << dev))) {
+        ST_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
+        if (dev >= 0 && dev < 64) attr_set |= 1ull << dev;
+    }
+    kern<<<ctas, kX3Threads, Cfg::kSmemBytes, stream>>>(ma, mb, kp);
+    note_launch();
+    const cudaError_t e = cudaPeekAtLastError();
+    return e == cudaSuccess ? ST_OK : cuda_fail(cudaGetLastError(), "gemm_tf32x3_kernel launch");
+}
+
 }  // namespace
+
+int plan_gemm_x3(int64_t m, int64_t n, bool b_n_contiguous, int sm_count, GemmPlan *plan) {
+    if (m <= 0 || n <= 0) return fail(ST_ERR_INVALID_ARGUMENT, "matmul extents must be positive");
+    if (sm_count <= 0) sm_count = 148;
+    GemmPlan best;
+    double best_score = -1.0;
+    const int cand[2] = {128, 64};
+    const double mma_eff[2] = {1.0, 0.88};
+    // an N-contiguous B needs a raw staging buffer: only block_n 64 keeps 4 stages
+    for (int i = b_n_contiguous ? 1 : 0; i < 2; ++i) {
+        const int bn = cand[i];
+        const int64_t tiles = cdiv(m, kBlockM) * cdiv(n, bn);
+        const int64_t waves = cdiv(tiles, sm_count);
+        const double fill = static_cast<double>(tiles) / static_cast<double>(waves * sm_count);
+        const double ncov = static_cast<double>(n) / static_cast<double>(cdiv(n, bn) * bn);
+        const double score = fill * ncov * mma_eff[i];
+        if (score > best_score + 1e-9) {
+            best_score = score;
+            best.block_n = bn;
+            best.tiles = static_cast<int>(tiles);
+        }
+    }
+    best.pair = false;
+    best.block_m = kBlockM;
+    best.block_k = 32;
+    best.stages = b_n_contiguous ? X3Cfg<64, true>::kStages
+                                 : (best.block_n == 128 ? X3Cfg<128, false>::kStages : X3Cfg<64, false>::kStages);
+    best.ctas = best.tiles < sm_count ? best.tiles : sm_count;
+    *plan = best;
+    return ST_OK;
+}
+
+int launch_gemm_3xtf32(const GemmArgs &g, int sm_count, int *dev_err, uint64_t timeout_ns, cudaStream_t stream) {
+    GemmPlan plan;
+    ST_TRY(plan_gemm_x3(g.m, g.n, !g.b_k_major, sm_count, &plan));
+    for (const void *ptr : {g.a, g.b})
+        if (reinterpret_cast<uintptr_t>(ptr) % 16 != 0)
+            return fail(ST_ERR_INVALID_ARGUMENT, "tensor-core operands must be 16-byte aligned");
+    if ((g.lda * 4) % 16 != 0 || (g.ldb * 4) % 16 != 0)
+        return fail(ST_ERR_INVALID_ARGUMENT, "tensor-core operand row strides must be multiples of 16 bytes");
+    CUtensorMap ma, mb;
+    ST_TRY(make_map(&ma, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, g.a, static_cast<uint64_t>(g.k), static_cast<uint64_t>(g.m),
+                    static_cast<uint64_t>(g.lda) * 4, 32, kBlockM));
+    if (g.b_k_major) {
+        ST_TRY(make_map(&mb, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, g.b, static_cast<uint64_t>(g.k),
+                        static_cast<uint64_t>(g.n), static_cast<uint64_t>(g.ldb) * 4, 32, plan.block_n));
+    } else {
+        ST_TRY(make_map(&mb, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, g.b, static_cast<uint64_t>(g.n),
+                        static_cast<uint64_t>(g.k), static_cast<uint64_t>(g.ldb) * 4, 32, 32));
+    }
+    KParams kp;
+    kp.m = static_cast<int>(g.m);
+    kp.n = static_cast<int>(g.n);
+    kp.k = static_cast<int>(g.k);
+    kp.num_m_tiles = static_cast<int>(cdiv(g.m, kBlockM));
+    kp.num_n_tiles = static_cast<int>(cdiv(g.n, plan.block_n));
+    kp.num_k_blocks = static_cast<int>(cdiv(g.k, 32));
+    kp.total_tiles = kp.num_m_tiles * kp.num_n_tiles;
+    kp.c = g.c;
+    kp.ldc = g.ldc;
+    kp.c_dtype = g.c_dtype;
+    kp.bias = g.bias;
+    kp.bias_dtype = g.bias_dtype;
+    kp.err = dev_err;
+    kp.timeout_ns = timeout_ns;
+    if (!g.b_k_major) return launch_x3_instance<true, 64>(ma, mb, kp, plan.ctas, stream);
+    if (plan.block_n == 128) return launch_x3_instance<false, 128>(ma, mb, kp, plan.ctas, stream);
+    return launch_x3_instance<false, 64>(ma, mb, kp, plan.ctas, stream);
+}
 
 int plan_gemm(int in_dtype, int64_t m, int64_t n, int64_t k, int sm_count, GemmPlan *plan) {
     if (m <= 0 || n <= 0 || k <= 0) return fail(ST_ERR_INVALID_ARGUMENT, "matmul extents must be positive");

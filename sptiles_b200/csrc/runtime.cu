@@ -16,6 +16,7 @@
 #include <atomic>
 #include <chrono>
 #include <cstdint>
+#include <cstdlib>
 #include <cstring>
 #include <string>
 #include <thread>
@@ -328,6 +329,25 @@ int matmul_device(const ExecCtx &x, const st_tensor &a, const st_tensor &b, cons
     g.n = N;
     Workspace &ws = x.dev->scratch;
     if (a.dtype == ST_F32) {
+        // Opt-in (SPTILES_B200_FP32_FUSED=1): split into tf32 hi/lo inside the
+        // GEMM.  Its 128 x 64 tiles are bound by shared-memory bandwidth, so the
+        // packed route below -- which can use the 256 x 256 CTA-pair kernel --
+        // is faster from 2048^3 up (218 vs 61 TFLOP/s at 4096^3) and ties at 1024^3.
+        const bool a_ok = (a.strides[1] == 1 || K == 1) && (a.strides[0] * 4) % 16 == 0 && aligned16(a.data);
+        const bool b_rows_ok = (b.strides[1] == 1 || N == 1) && (b.strides[0] * 4) % 16 == 0 && aligned16(b.data);
+        const bool b_cols_ok = (b.strides[0] == 1 || K == 1) && (b.strides[1] * 4) % 16 == 0 && aligned16(b.data);
+        const char *fused = std::getenv("SPTILES_B200_FP32_FUSED");
+        if (fused && fused[0] == '1' && a_ok && (b_rows_ok || b_cols_ok)) {
+            g.ab_dtype = ST_F32;
+            g.a = a.data;
+            g.lda = a.strides[0];
+            g.b = b.data;
+            g.b_k_major = !b_rows_ok;
+            g.ldb = b_rows_ok ? b.strides[0] : b.strides[1];
+            g.k = K;
+            return launch_gemm_3xtf32(g, x.dev->sm_count, x.dev->dev_err, kDeviceWaitLimitNs, x.stream);
+        }
+        // otherwise pack [hi|hi|lo] x [hi;lo;hi] into scratch and run one tf32 GEMM
         const int64_t kp = tf32_packed_k(K);
         const size_t need = static_cast<size_t>(M + N) * 3 * kp * sizeof(float);
         void *base = nullptr;

@@ -327,3 +327,37 @@ def test_calls_replay_from_a_cuda_graph(dtype):
     g.replay()
     torch.cuda.synchronize()
     assert out.cpu().numpy().tobytes() == oracle.matmul_kat_expected(m, n, k).tobytes()
+
+
+# ------------------------------------------------------------ fp32: split in the kernel vs packed operands
+@pytest.mark.parametrize("path", ["fused", "prepack"])
+@pytest.mark.parametrize("mnk", [(64, 64, 64), (100, 72, 36), (300, 520, 200), (1000, 24, 520), (516, 780, 132),
+                                 (1024, 1024, 1024), (100, 70, 33)])
+def test_fp32_paths_known_answers(monkeypatch, path, mnk):
+    """The default route packs [hi|hi|lo] x [hi;lo;hi] and runs one tf32 GEMM;
+    the opt-in fused kernel splits TMA-staged fp32 tiles in shared memory."""
+    if path == "fused":
+        monkeypatch.setenv("SPTILES_B200_FP32_FUSED", "1")
+    else:
+        monkeypatch.delenv("SPTILES_B200_FP32_FUSED", raising=False)
+    m, n, k = mnk
+    A, B = kat(m, n, k, torch.float32)
+    want = oracle.matmul_kat_expected(m, n, k).tobytes()
+    assert st.matmul(A, B).cpu().numpy().tobytes() == want
+    assert st.matmul(A, B.t().contiguous().t()).cpu().numpy().tobytes() == want  # column-major B
+
+
+@pytest.mark.parametrize("path", ["fused", "prepack"])
+def test_fp32_paths_random_accuracy(monkeypatch, path):
+    if path == "fused":
+        monkeypatch.setenv("SPTILES_B200_FP32_FUSED", "1")
+    else:
+        monkeypatch.delenv("SPTILES_B200_FP32_FUSED", raising=False)
+    m, n, k = 768, 640, 1000
+    A, B = normal((m, k), 1.0, 80, torch.float32), normal((k, n), 1.0, 81, torch.float32)
+    bias = normal((n,), 1.0, 82, torch.float32)
+    want = oracle_mm(A, B, bias)
+    for Bv in (B, B.t().contiguous().t()):
+        C = st.matmul(A, Bv, bias)
+        err = rel_err(C.cpu().numpy(), want)
+        assert err <= 5e-5, f"{path}: 3xTF32 error {err}"
