@@ -135,6 +135,10 @@ int st_download(st_ctx *ctx, int32_t device, void *dst, const void *src, uint64_
  *   "persistent_matmul_fp32", "persistent_matmul_f16", "persistent_matmul_bf16"
  *                           persistent-kernel semantics (matmul.py:106-178):
  *                           any grid >= 1 covers every output tile
+ *   "vector_fma"            A,B,D,C rank 1 f32 (12 params) [+ tile_size]: C = fma(A, B, D)
+ *   "vector_fma_2d"         A,B,D,C rank 2 f32 (20 params) [+ tile_m, tile_n]
+ *   "cast"                  A,C rank 1 (6 params) [+ tile_size]: C = A in C's dtype
+ *   "cast_2d"               A,C rank 2 (10 params) [+ tile_m, tile_n]
  * grid counts tile blocks.  A matmul grid must cover every output tile
  * (cdiv(M,tm)*cdiv(N,tn) blocks) unless the entry is persistent; a
  * vector_add grid may cover fewer tiles, and only those are computed. */
@@ -157,6 +161,14 @@ int st_vector_add(st_ctx *ctx, const st_tensor *a, const st_tensor *b, const st_
  * f16 or bf16; bias (may be NULL) is f32 or the input type. */
 int st_matmul(st_ctx *ctx, const st_tensor *a, const st_tensor *b, const st_tensor *bias,
               const st_tensor *c, const st_exec *exec);
+
+/* C = fma(A, B, D) elementwise: A*B + D rounded once (f32, rank 1 or 2,
+ * any strides) -- the lowering's fma (tileops.hpp:616-623). */
+int st_vector_fma(st_ctx *ctx, const st_tensor *a, const st_tensor *b, const st_tensor *d, const st_tensor *c,
+                  const st_exec *exec);
+/* C = A converted to C's dtype (ST_F32 / ST_F16 / ST_BF16; round to nearest
+ * even when narrowing) -- the lowering's ftof (tileops.hpp:257-258). */
+int st_cast(st_ctx *ctx, const st_tensor *a, const st_tensor *c, const st_exec *exec);
 
 /* ---- typed calls on host memory: copy in, compute, copy out, all on the
  *      context's stream; returns once C is back in host memory. ---- */

@@ -355,3 +355,41 @@ void or_kat_values(float *out, int64_t count, int64_t modulus, int64_t offset, f
 void or_kat_iota(float *out, int64_t count, int64_t start) {
     for (int64_t i = 0; i < count; ++i) out[i] = (float)(start + i);
 }
+
+/* ------------------------------------------------------------------------ */
+/* fma: elementwise fused multiply-add (tileops.hpp:616-623).               */
+/* ------------------------------------------------------------------------ */
+
+/*
+ * C[i] = fma(A[i], B[i], D[i]) for i < min(grid_tiles * tile, C.size).  The
+ * lowering emits GLSL.std.450 Fma (materialize_fma, tileops.hpp:616-623);
+ * this restatement uses the IEEE-754 fused operation, a*b+d rounded once to
+ * nearest even (C99 fmaf).  Tile coverage is that of the tile add.
+ */
+int or_vector_fma_1d(const float *a, int64_t a_size, int64_t a_stride, const float *b, int64_t b_size,
+                     int64_t b_stride, const float *d, int64_t d_size, int64_t d_stride, float *c, int64_t c_size,
+                     int64_t c_stride, int64_t tile, int64_t grid_tiles) {
+    if (tile <= 0 || grid_tiles < 0) return OR_ERR_ARG;
+    int64_t end = grid_tiles * tile;
+    if (end > c_size) end = c_size;
+    if (end > a_size || end > b_size || end > d_size) return OR_ERR_ARG;
+    for (int64_t i = 0; i < end; ++i) c[i * c_stride] = fmaf(a[i * a_stride], b[i * b_stride], d[i * d_stride]);
+    return OR_OK;
+}
+
+/* ------------------------------------------------------------------------ */
+/* ftof: elementwise floating-point conversion (tileops.hpp:257-258).       */
+/* ------------------------------------------------------------------------ */
+
+/*
+ * C[i] = (out type) A[i] for i < n, element strides in elements.  The
+ * reference lowering passes ftof through unchanged (its path is f32-only,
+ * tileops.hpp:257-258), which is the f32 -> f32 case here; the narrowing
+ * conversions round to nearest even, widening ones are exact.
+ */
+int or_cast(int in_dtype, const void *a, int64_t a_stride, int out_dtype, void *c, int64_t c_stride, int64_t n) {
+    if (in_dtype < OR_F32 || in_dtype > OR_BF16 || out_dtype < OR_F32 || out_dtype > OR_BF16 || n < 0)
+        return OR_ERR_ARG;
+    for (int64_t i = 0; i < n; ++i) store_elem(out_dtype, c, i * c_stride, load_elem(in_dtype, a, i * a_stride));
+    return OR_OK;
+}

@@ -19,7 +19,7 @@ __all__ = [
     "lib", "vector_add_1d", "vector_add_2d", "matmul", "reference_matmul_f32",
     "f32_to_bf16_bits", "bf16_bits_to_f32", "f32_to_f16_bits", "f16_bits_to_f32",
     "kat_values", "kat_iota", "matmul_kat_expected", "time_matmul_rows",
-    "time_vector_add",
+    "time_vector_add", "vector_fma_1d", "cast",
 ]
 
 F32, F16, BF16 = 0, 1, 2
@@ -62,6 +62,10 @@ def lib() -> ctypes.CDLL:
     L.or_kat_values.restype = None
     L.or_kat_iota.argtypes = [_vp, _i64, _i64]
     L.or_kat_iota.restype = None
+    L.or_vector_fma_1d.argtypes = [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _i64, _i64]
+    L.or_vector_fma_1d.restype = ctypes.c_int
+    L.or_cast.argtypes = [ctypes.c_int, _vp, _i64, ctypes.c_int, _vp, _i64, _i64]
+    L.or_cast.restype = ctypes.c_int
     L.or_f16_to_f32.argtypes = [ctypes.c_uint16]
     L.or_f16_to_f32.restype = ctypes.c_float
     L.or_bf16_to_f32.argtypes = [ctypes.c_uint16]
@@ -91,6 +95,29 @@ def vector_add_1d(a: np.ndarray, b: np.ndarray, c: np.ndarray, tile: int, grid_t
     if rc:
         raise ValueError(f"or_vector_add_1d failed ({rc})")
     return c
+
+
+def vector_fma_1d(a: np.ndarray, b: np.ndarray, d: np.ndarray, c: np.ndarray, tile: int, grid_tiles: int) -> np.ndarray:
+    """C[i] = fma(A[i], B[i], D[i]) (one rounding) over the tiles the grid covers; C updated in place."""
+    for x in (a, b, d, c):
+        assert x.dtype == np.float32 and x.ndim == 1
+    rc = lib().or_vector_fma_1d(_ptr(a), a.shape[0], _estrides(a)[0], _ptr(b), b.shape[0], _estrides(b)[0],
+                                _ptr(d), d.shape[0], _estrides(d)[0], _ptr(c), c.shape[0], _estrides(c)[0],
+                                tile, grid_tiles)
+    if rc:
+        raise ValueError(f"or_vector_fma_1d failed ({rc})")
+    return c
+
+
+def cast(a: np.ndarray, out_dtype: int, *, bf16_in: bool = False) -> np.ndarray:
+    """Elementwise conversion of a 1D array to F32 / F16 / BF16 (BF16 as uint16 bit patterns)."""
+    a = np.ascontiguousarray(a).reshape(-1)
+    in_code = _dtype_code(a, bf16_in)
+    out = np.zeros(a.shape[0], dtype={F32: np.float32, F16: np.float16, BF16: np.uint16}[out_dtype])
+    rc = lib().or_cast(in_code, _ptr(a), 1, out_dtype, _ptr(out), 1, a.shape[0])
+    if rc:
+        raise ValueError(f"or_cast failed ({rc})")
+    return out
 
 
 def vector_add_2d(a: np.ndarray, b: np.ndarray, c: np.ndarray, tm: int, tn: int, grid_x: int, grid_y: int) -> np.ndarray:

@@ -8,8 +8,8 @@ Python host side: it mirrors the reference's operator API
 and its runner (shaders/spirv_runtime.py).
 """
 from .api import (  # noqa: F401
-    MATMUL_TILE_M, MATMUL_TILE_N, VECTOR_ADD_TILE_SIZE, cutile_matmul, cutile_matmul_spirv, matmul,
-    spirv_matmul, spirv_vector_add, tensor_view, vector_add,
+    MATMUL_TILE_M, MATMUL_TILE_N, VECTOR_ADD_TILE_SIZE, cast, cutile_matmul, cutile_matmul_spirv, matmul,
+    spirv_matmul, spirv_vector_add, tensor_view, vector_add, vector_fma,
 )
 from .runtime import (  # noqa: F401
     LOCAL_SIZE_X, ceil_div, context, device_count, grid_from_dispatch, kernel_launches, matmul_plan,

@@ -115,6 +115,39 @@ def spirv_vector_add(A: torch.Tensor, B: torch.Tensor, *, spirv_path: str | Path
     return vector_add(A, B)
 
 
+def vector_fma(A: torch.Tensor, B: torch.Tensor, D: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """C = A * B + D elementwise with one rounding (f32 CUDA tensors, rank 1 or 2, any strides).
+
+    The lowering's `fma` (tileops.hpp:616-623, GLSL.std.450 Fma) as a fused
+    IEEE multiply-add.
+    """
+    if not (A.shape == B.shape == D.shape):
+        raise ValueError(f"Input tensors must have the same shape: {A.shape}, {B.shape}, {D.shape}")
+    if not (A.device == B.device == D.device) or not A.is_cuda:
+        raise ValueError("Input tensors must be on the same CUDA device.")
+    C = out if out is not None else torch.empty(A.shape, dtype=A.dtype, device=A.device)
+    ex = _exec_for(A)
+    va, vb, vd, vc = tensor_view(A), tensor_view(B), tensor_view(D), tensor_view(C)
+    N.check(N.lib().st_vector_fma(_ctx(ex), ctypes.byref(va), ctypes.byref(vb), ctypes.byref(vd), ctypes.byref(vc),
+                                  ctypes.byref(ex)), "vector_fma")
+    return C
+
+
+def cast(A: torch.Tensor, dtype: torch.dtype, out: torch.Tensor | None = None) -> torch.Tensor:
+    """A converted to ``dtype`` (float32 / float16 / bfloat16) on the GPU, round to nearest even.
+
+    The lowering's `ftof` (tileops.hpp:257-258), which the f32-only
+    reference passes through unchanged.
+    """
+    if not A.is_cuda:
+        raise ValueError("Input tensor must be on a CUDA device.")
+    C = out if out is not None else torch.empty(A.shape, dtype=dtype, device=A.device)
+    ex = _exec_for(A)
+    va, vc = tensor_view(A), tensor_view(C)
+    N.check(N.lib().st_cast(_ctx(ex), ctypes.byref(va), ctypes.byref(vc), ctypes.byref(ex)), "cast")
+    return C
+
+
 # ----------------------------------------------------------------- matmul
 def matmul(A: torch.Tensor, B: torch.Tensor, bias: torch.Tensor | None = None, *,
            out_dtype: torch.dtype | None = None, out: torch.Tensor | None = None) -> torch.Tensor:

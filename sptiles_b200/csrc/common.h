@@ -58,6 +58,14 @@ int launch_vector_add_1d(const float *a, int64_t sa, const float *b, int64_t sb,
 int launch_vector_add_2d(const float *a, const int64_t sa[2], const float *b, const int64_t sb[2], float *c,
                          const int64_t sc[2], int64_t rows, int64_t cols, int sm_count, cudaStream_t stream);
 
+// C = fma(A, B, D) elementwise (f32), 2D strides; a rank-1 view is one row.
+int launch_vector_fma(const float *a, const int64_t sa[2], const float *b, const int64_t sb[2], const float *d,
+                      const int64_t sd[2], float *c, const int64_t sc[2], int64_t rows, int64_t cols, int sm_count,
+                      cudaStream_t stream);
+// C = A converted to C's dtype (ST_F32 / ST_F16 / ST_BF16), 2D strides.
+int launch_cast(const void *a, int a_dtype, const int64_t sa[2], void *c, int c_dtype, const int64_t sc[2],
+                int64_t rows, int64_t cols, int sm_count, cudaStream_t stream);
+
 // Tensor-core GEMM plan.
 struct GemmPlan {
     bool pair = false;  // CTA-pair kernel (cta_group::2): block_m 256, block_n 256

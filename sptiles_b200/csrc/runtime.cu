@@ -618,7 +618,7 @@ int vector_add_host_pipelined(const ExecCtx &x, const st_tensor &a, const st_ten
 }
 
 // ------------------------------------------------------------ entry registry
-enum class Kind { VectorAdd1D, VectorAdd2D, Matmul };
+enum class Kind { VectorAdd1D, VectorAdd2D, Matmul, Fma1D, Fma2D, Cast1D, Cast2D };
 
 struct Entry {
     const char *name;
@@ -644,6 +644,11 @@ const Entry kEntries[] = {
     {"persistent_matmul_fp32", Kind::Matmul, ST_F32, false, true, 3, {32, 32, 32}},
     {"persistent_matmul_f16", Kind::Matmul, ST_F16, false, true, 3, {128, 256, 64}},
     {"persistent_matmul_bf16", Kind::Matmul, ST_BF16, false, true, 3, {128, 256, 64}},
+    // the other elementwise ops the lowering materialises (tileops.hpp:616-623, 257-258)
+    {"vector_fma", Kind::Fma1D, ST_F32, false, false, 1, {1024, 0, 0}},
+    {"vector_fma_2d", Kind::Fma2D, ST_F32, false, false, 2, {64, 64, 0}},
+    {"cast", Kind::Cast1D, ST_F32, false, false, 1, {1024, 0, 0}},
+    {"cast_2d", Kind::Cast2D, ST_F32, false, false, 2, {64, 64, 0}},
 };
 
 const Entry *find_entry(const char *name) {
@@ -657,11 +662,17 @@ const Entry *find_entry(const char *name) {
 // rank 1 = (data, size, stride); rank 2 = (data, dim0, dim1, stride0, stride1).
 int parse_params(const Entry &e, const st_param *params, int n_params, std::vector<st_tensor> *views,
                  std::vector<int> *buffer_index, int consts[3]) {
-    const int n_arrays = (e.kind == Kind::Matmul) ? (e.bias ? 4 : 3) : 3;
     std::vector<int> ranks;
-    if (e.kind == Kind::VectorAdd1D) ranks = {1, 1, 1};
-    else if (e.kind == Kind::VectorAdd2D) ranks = {2, 2, 2};
-    else ranks = e.bias ? std::vector<int>{2, 2, 2, 1} : std::vector<int>{2, 2, 2};
+    switch (e.kind) {
+    case Kind::VectorAdd1D: ranks = {1, 1, 1}; break;
+    case Kind::VectorAdd2D: ranks = {2, 2, 2}; break;
+    case Kind::Fma1D: ranks = {1, 1, 1, 1}; break;   // A, B, D, C
+    case Kind::Fma2D: ranks = {2, 2, 2, 2}; break;
+    case Kind::Cast1D: ranks = {1, 1}; break;         // A, C
+    case Kind::Cast2D: ranks = {2, 2}; break;
+    case Kind::Matmul: ranks = e.bias ? std::vector<int>{2, 2, 2, 1} : std::vector<int>{2, 2, 2}; break;
+    }
+    const int n_arrays = static_cast<int>(ranks.size());
     int pos = 0;
     for (int i = 0; i < n_arrays; ++i) {
         const int r = ranks[i];
@@ -735,6 +746,40 @@ int run_entry(const ExecCtx &x, const Entry &e, const st_grid &grid, std::vector
                                     static_cast<const float *>(v[1].data), v[1].strides,
                                     static_cast<float *>(v[2].data), v[2].strides, rows, cols, x.dev->sm_count,
                                     x.stream);
+    }
+    if (e.kind == Kind::Fma1D || e.kind == Kind::Cast1D || e.kind == Kind::Fma2D || e.kind == Kind::Cast2D) {
+        const bool fma = e.kind == Kind::Fma1D || e.kind == Kind::Fma2D;
+        const size_t n_in = fma ? 3 : 1;
+        st_tensor &out = v[n_in];
+        if (fma)
+            for (size_t i = 0; i <= n_in; ++i)
+                if (v[i].dtype != ST_F32) return fail(ST_ERR_INVALID_ARGUMENT, std::string(e.name) + " is f32-only");
+        int64_t rows, cols;
+        if (out.rank == 1) {
+            rows = 1;
+            cols = std::min<int64_t>(blocks * consts[0], out.shape[0]);
+            for (size_t i = 0; i < n_in; ++i)
+                if (cols > v[i].shape[0])
+                    return fail(ST_ERR_INVALID_ARGUMENT, std::string(e.name) + ": inputs must cover every stored element");
+        } else {
+            rows = std::min<int64_t>(static_cast<int64_t>(grid.x) * consts[0], out.shape[0]);
+            cols = std::min<int64_t>(static_cast<int64_t>(grid.y) * consts[1], out.shape[1]);
+            if (grid.z == 0) rows = 0;
+            for (size_t i = 0; i < n_in; ++i)
+                if (rows > v[i].shape[0] || cols > v[i].shape[1])
+                    return fail(ST_ERR_INVALID_ARGUMENT, std::string(e.name) + ": inputs must cover every stored element");
+        }
+        int64_t s[4][2];
+        for (size_t i = 0; i <= n_in; ++i) {
+            s[i][0] = v[i].rank == 1 ? cols : v[i].strides[0];
+            s[i][1] = v[i].rank == 1 ? v[i].strides[0] : v[i].strides[1];
+        }
+        if (fma)
+            return launch_vector_fma(static_cast<const float *>(v[0].data), s[0], static_cast<const float *>(v[1].data),
+                                     s[1], static_cast<const float *>(v[2].data), s[2], static_cast<float *>(v[3].data),
+                                     s[3], rows, cols, x.dev->sm_count, x.stream);
+        return launch_cast(v[0].data, v[0].dtype, s[0], v[1].data, v[1].dtype, s[1], rows, cols, x.dev->sm_count,
+                           x.stream);
     }
     const st_tensor *bias = e.bias ? &v[3] : nullptr;
     ST_TRY(check_matmul(&v[0], &v[1], bias, &v[2]));
@@ -950,7 +995,11 @@ int st_launch(st_ctx *ctx, const char *entry_name, const st_grid *grid, const st
         cursor += (p.bytes + 255) & ~uint64_t(255);
     }
     ST_TRY(run_entry(x, *e, *grid, dev_views, consts));
-    const int32_t default_out[1] = {bufpos[2]};
+    // default output: C, the third array of the add/matmul signatures, the last one otherwise
+    const int32_t default_out[1] = {(e->kind == Kind::VectorAdd1D || e->kind == Kind::VectorAdd2D ||
+                                     e->kind == Kind::Matmul)
+                                        ? bufpos[2]
+                                        : bufpos.back()};
     const int32_t *outs = exec && exec->n_outputs > 0 ? exec->output_indices : default_out;
     const int n_outs = exec && exec->n_outputs > 0 ? exec->n_outputs : 1;
     for (int i = 0; i < n_outs; ++i) {
@@ -984,6 +1033,48 @@ int st_matmul(st_ctx *ctx, const st_tensor *a, const st_tensor *b, const st_tens
     ST_TRY(check_matmul(a, b, bias, c));
     DeviceGuard guard(x.dev->ordinal);
     ST_TRY(matmul_device(x, *a, *b, bias, *c));
+    return finish(x);
+}
+
+int st_vector_fma(st_ctx *ctx, const st_tensor *a, const st_tensor *b, const st_tensor *d, const st_tensor *c,
+                  const st_exec *exec) {
+    ExecCtx x;
+    ST_TRY(resolve_exec(ctx, exec, &x));
+    ST_TRY(check_vector_add(a, b, c));
+    ST_TRY(check_vector_add(a, d, c));
+    DeviceGuard guard(x.dev->ordinal);
+    const int64_t rows = c->rank == 2 ? c->shape[0] : 1;
+    const int64_t cols = c->rank == 2 ? c->shape[1] : c->shape[0];
+    int64_t s[4][2];
+    const st_tensor *t[4] = {a, b, d, c};
+    for (int i = 0; i < 4; ++i) {
+        s[i][0] = t[i]->rank == 1 ? cols : t[i]->strides[0];
+        s[i][1] = t[i]->rank == 1 ? t[i]->strides[0] : t[i]->strides[1];
+    }
+    ST_TRY(launch_vector_fma(static_cast<const float *>(a->data), s[0], static_cast<const float *>(b->data), s[1],
+                             static_cast<const float *>(d->data), s[2], static_cast<float *>(c->data), s[3], rows, cols,
+                             x.dev->sm_count, x.stream));
+    return finish(x);
+}
+
+int st_cast(st_ctx *ctx, const st_tensor *a, const st_tensor *c, const st_exec *exec) {
+    ExecCtx x;
+    ST_TRY(resolve_exec(ctx, exec, &x));
+    if (!a || !c) return fail(ST_ERR_INVALID_ARGUMENT, "cast: null tensor");
+    if (c->rank != 1 && c->rank != 2) return fail(ST_ERR_INVALID_ARGUMENT, "cast: tensors must be rank 1 or 2");
+    ST_TRY(check_view(a, "A", c->rank));
+    ST_TRY(check_view(c, "C", c->rank));
+    for (const st_tensor *t : {a, c})
+        if (t->dtype != ST_F32 && t->dtype != ST_F16 && t->dtype != ST_BF16)
+            return fail(ST_ERR_INVALID_ARGUMENT, "cast: tensors must be ST_F32, ST_F16 or ST_BF16");
+    for (int i = 0; i < c->rank; ++i)
+        if (a->shape[i] != c->shape[i]) return fail(ST_ERR_INVALID_ARGUMENT, "cast: A and C must have the same shape");
+    DeviceGuard guard(x.dev->ordinal);
+    const int64_t rows = c->rank == 2 ? c->shape[0] : 1;
+    const int64_t cols = c->rank == 2 ? c->shape[1] : c->shape[0];
+    const int64_t sa[2] = {a->rank == 1 ? cols : a->strides[0], a->rank == 1 ? a->strides[0] : a->strides[1]};
+    const int64_t sc[2] = {c->rank == 1 ? cols : c->strides[0], c->rank == 1 ? c->strides[0] : c->strides[1]};
+    ST_TRY(launch_cast(a->data, a->dtype, sa, c->data, c->dtype, sc, rows, cols, x.dev->sm_count, x.stream));
     return finish(x);
 }
 
