@@ -62,6 +62,10 @@ def parse_args():
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--no-secondary", action="store_true", help="skip the vector_add measurement of the default run")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--replicate", choices=["fused", "nccl"], default=None,
+                   help="matmul: every step leaves the full C on every rank. fused: the GEMM epilogue stores each "
+                        "C chunk into every rank's copy over NVLink peer memory; nccl: the GEMM, then an NCCL "
+                        "all-gather of the row blocks")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--timing", choices=["auto", "graph", "eager"], default="auto",
                    help="graph: replay the K timed steps from one CUDA graph (host launch overhead out of the "
@@ -263,7 +267,7 @@ def sum_over_ranks(x, dist_on):
 def run_matmul(wl, args, rank, world, local, dist_on, peaks):
     import torch
     import sptiles_b200 as st
-    from sptiles_b200.partition import matmul_row_shard
+    from sptiles_b200.partition import gather_row_shards, matmul_row_shard
 
     dev = torch.device("cuda", local)
     r0, r1 = matmul_row_shard(wl["m"], world, rank)
@@ -273,16 +277,58 @@ def run_matmul(wl, args, rank, world, local, dist_on, peaks):
     c = torch.empty((rows, wl["n"]), dtype=out_dt, device=dev)
     stream = torch.cuda.current_stream(dev)
 
+    replicate = args.replicate if dist_on else None
+    c_full = torch.empty((wl["m"], wl["n"]), dtype=out_dt, device=dev) if replicate else None
+    rep = None
+    if replicate == "fused":
+        from sptiles_b200.partition import ReplicatedOutput
+        rep = ReplicatedOutput(wl["m"], wl["n"], out_dt)
+
     def step(_i):
+        if rep is not None:
+            rep.matmul(a, b, bias)
+            return
         if rows:
             st.matmul(a, b, bias, out=c)
+        if replicate:
+            gather_row_shards(c, wl["m"], out=c_full)
 
     with ClockSampler(local) as clk:
-        ms, launches = time_steps(step, args.steps, args.warmup, stream, dist_on, graph=use_graph(args, wl))
+        ms, launches = time_steps(step, args.steps, args.warmup, stream, dist_on,
+                                  graph=use_graph(args, wl) and not replicate)
     ms_max = max_over_ranks(ms, dist_on)
+    gather = None
+    kernel_ms = ms  # this rank's device time of the GEMM launches alone
+    if replicate:
+        def gemm_only(_i):
+            if rows:
+                st.matmul(a, b, bias, out=c)
+
+        def gather_only(_i):
+            gather_row_shards(c, wl["m"], out=c_full)
+
+        def gemm_then_nccl(_i):
+            gemm_only(_i)
+            gather_only(_i)
+        kernel_ms, _ = time_steps(gemm_only, args.steps, 2, stream, dist_on, graph=False)
+        g_ms, _ = time_steps(gather_only, args.steps, 2, stream, dist_on, graph=False)
+        g_ms = max_over_ranks(g_ms, dist_on) / args.steps
+        gemm_ms = max_over_ranks(kernel_ms, dist_on) / args.steps
+        recv = (wl["m"] - rows) * wl["n"] * c.element_size()
+        gather = {"mode": replicate, "step_ms": round(ms_max / args.steps, 4), "gemm_alone_ms": round(gemm_ms, 4),
+                  "nccl_allgather_alone_ms": round(g_ms, 4), "bytes_received_per_rank": int(recv),
+                  "nccl_GBps_per_rank": round(recv / (g_ms / 1e3) / 1e9, 1)}
+        if replicate == "fused":
+            n_ms, _ = time_steps(gemm_then_nccl, args.steps, 2, stream, dist_on, graph=False)
+            gather["gemm_then_nccl_step_ms"] = round(max_over_ranks(n_ms, dist_on) / args.steps, 4)
+            gather["how"] = ("the GEMM epilogue stores each C chunk into every rank's copy (CUDA IPC peer "
+                             "pointers over NVLink), then a one-element NCCL all-reduce orders the ranks")
+        else:
+            gather["how"] = "the GEMM, then torch.distributed.all_gather_into_tensor (NCCL) of the C row blocks"
+        gather["overhead_over_gemm_ms"] = round(ms_max / args.steps - gemm_ms, 4)
     total_flops = sum_over_ranks(flops_of(wl, rows), dist_on)
     value = total_flops * args.steps / (ms_max / 1e3) / 1e12
-    per_launch_ms = ms / args.steps
+    per_launch_ms = kernel_ms / args.steps
     achieved = flops_of(wl, rows) / (per_launch_ms / 1e3) / 1e12 if rows else 0.0
     peak = peaks["bf16_tflops"]
     if wl["dtype"] == "f32":
@@ -297,7 +343,9 @@ def run_matmul(wl, args, rank, world, local, dist_on, peaks):
             if peaks["source"] == "measured" else "of fallback peak",
             "traffic": traffic, "kernel": "gemm_tc_kernel", "ms_per_launch": round(per_launch_ms, 4)}
     out = dict(value=value, ms_per_step=ms_max / args.steps, roofline=roof, gpu_launches=int(launches),
-               clocks=clk.summary(), plan=plan, rows=rows)
+               clocks=clk.summary(), plan=plan, rows=rows, allgather=gather)
+    if rep is not None:
+        rep.close()
     if not args.no_e2e:
         out["e2e"] = e2e_matmul(wl, args, a, b, bias, out_dt, rows, dist_on)
     return out
@@ -585,6 +633,9 @@ def main():
             if wl["kind"] == "matmul":
                 line["config"]["tile"] = f"{res['plan']['block_m']}x{res['plan']['block_n']}x{res['plan']['block_k']}"
                 line["config"]["ctas"] = res["plan"]["ctas"]
+                if args.replicate and world > 1:
+                    line["config"]["replicate_output"] = args.replicate
+                    line["allgather"] = res.get("allgather")
             if secondary:
                 line["vecadd"] = secondary
             print(json.dumps(line), flush=True)

@@ -177,6 +177,28 @@ int st_vector_add_host(st_ctx *ctx, const st_tensor *a, const st_tensor *b, cons
 int st_matmul_host(st_ctx *ctx, const st_tensor *a, const st_tensor *b, const st_tensor *bias,
                    const st_tensor *c, const st_exec *exec);
 
+/* ---- one process per GPU: replicated C written by the GEMM epilogue ----
+ * The reference runs on one device (examples.cpp:115-131); these calls back
+ * the single-box partitioner.  st_ipc_handle exports a device allocation
+ * made by st_alloc; st_ipc_open maps another process's allocation on this
+ * GPU (over NVLink on the B200 box); st_ipc_close unmaps it.
+ * st_matmul_allgather computes C rows [row_offset, row_offset + rows(A)) =
+ * A @ B (+ bias) and its epilogue stores every finished chunk both into
+ * c_full (this GPU's [M, N] copy) and, over peer memory, into each of the
+ * n_peers (<= 7) other copies at the same offset -- the GEMM and the
+ * all-gather of C in one kernel (16-bit A/B: TMA stores of 32-row boxes when
+ * every copy's base and row stride are 16-byte multiples).  The other ranks'
+ * rows arrive in c_full once every rank's call has completed (e.g. after a
+ * collective on the same stream); the caller also orders the call after
+ * every reader of the previous contents of the other copies.  With K = 0
+ * the call returns ST_ERR_UNSUPPORTED. */
+int st_ipc_handle(st_ctx *ctx, int32_t device, void *ptr, uint8_t handle[64]);
+int st_ipc_open(st_ctx *ctx, int32_t device, const uint8_t handle[64], void **out);
+int st_ipc_close(st_ctx *ctx, int32_t device, void *ptr);
+int st_matmul_allgather(st_ctx *ctx, const st_tensor *a, const st_tensor *b, const st_tensor *bias,
+                        const st_tensor *c_full, void *const *peer_c_full, int32_t n_peers, int64_t row_offset,
+                        const st_exec *exec);
+
 /* ---- fp32 matmul that allocates nothing ----
  * No counterpart in the reference.  For callers that must not allocate
  * device memory: a process whose memory pool already holds the GPU's memory,

@@ -34,6 +34,7 @@ EXPORTED = (
     "st_alloc", "st_free", "st_upload", "st_download", "st_launch", "st_grid_from_dispatch",
     "st_vector_add", "st_matmul", "st_vector_add_host", "st_matmul_host", "st_tile_raster",
     "st_matmul_plan", "st_shard_range", "st_matmul_static_scratch", "st_vector_fma", "st_cast",
+    "st_ipc_handle", "st_ipc_open", "st_ipc_close", "st_matmul_allgather",
 )
 
 
@@ -99,6 +100,11 @@ def _declare(L: ctypes.CDLL) -> None:
         "st_matmul_host": ([vp, _P(StTensor), _P(StTensor), _P(StTensor), _P(StTensor), _P(StExec)], _c.c_int),
         "st_vector_fma": ([vp, _P(StTensor), _P(StTensor), _P(StTensor), _P(StTensor), _P(StExec)], _c.c_int),
         "st_cast": ([vp, _P(StTensor), _P(StTensor), _P(StExec)], _c.c_int),
+        "st_ipc_handle": ([vp, i32, vp, _P(_c.c_uint8)], _c.c_int),
+        "st_ipc_open": ([vp, i32, _P(_c.c_uint8), _P(vp)], _c.c_int),
+        "st_ipc_close": ([vp, i32, vp], _c.c_int),
+        "st_matmul_allgather": ([vp, _P(StTensor), _P(StTensor), _P(StTensor), _P(StTensor), _P(vp), i32, i64,
+                                 _P(StExec)], _c.c_int),
         "st_tile_raster": ([i64, i64, i64, i64, i64, i64, _P(i64), _P(i64)], _c.c_int),
         "st_matmul_plan": ([i32, i64, i64, i64, i32, _P(i32), _P(i32), _P(i32), _P(i32), _P(i32)], _c.c_int),
         "st_shard_range": ([i64, i32, i32, i64, _P(i64), _P(i64)], _c.c_int),

@@ -85,7 +85,16 @@ int plan_gemm(int in_dtype, int64_t m, int64_t n, int64_t k, int sm_count, GemmP
 //   B: if b_k_major, [N, K] row-major (K contiguous), row stride ldb;
 //      else [K, N] row-major (N contiguous), row stride ldb.
 //   C: [M, N] with row stride ldc, element type c_dtype; bias[N] optional.
+// Other GPUs' copies of C (CUDA IPC mappings over NVLink): the epilogue
+// writes every finished chunk to each of them at the same offset as locally.
+constexpr int kMaxPeers = 7;
+struct PeerOutputs {
+    void *base[kMaxPeers] = {};  // element (0, 0) of this call's C in each peer's copy
+    int n = 0;
+};
+
 struct GemmArgs {
+    PeerOutputs peers;
     int ab_dtype;
     const void *a;
     int64_t lda;

@@ -59,10 +59,19 @@ constexpr int kEpilogueWarps = 4;
 #ifndef ST_GROUP_M
 #define ST_GROUP_M 8
 #endif
+#ifndef ST_C_STORE_DEFAULT
+#define ST_C_STORE_DEFAULT 1  // local C: 1 TMA-store epilogue, 0 per-lane direct stores
+#endif
 #ifndef ST_C_POLICY
 #define ST_C_POLICY 0  // C stores: 0 default, 1 L2 evict_first
 #endif
 constexpr int kGroupM = ST_GROUP_M;
+
+// C staging for the TMA-store epilogue: per epilogue warp two buffers of one
+// 32-row x 128-byte box (32 fp32 or 64 16-bit columns), 128-byte swizzled.
+constexpr int kStageBoxBytes = 32 * 128;
+constexpr int kCStagingBytes = kEpilogueWarps * 2 * kStageBoxBytes;
+constexpr int kBarRegion = 1024;  // barriers + TMEM slot + abort flag; keeps the staging 1024-aligned
 
 template <int BN>
 struct TileCfg {
@@ -71,14 +80,17 @@ struct TileCfg {
     static constexpr int kStageBytes = kABytes + kBBytes;
     static constexpr int kStages = BN == 256 ? 4 : (BN == 128 ? 6 : 8);
     static constexpr int kTmemCols = 2 * BN;  // two accumulators; 128, 256 or 512 (powers of two)
-    static constexpr int kBarBytes = 256;
-    static constexpr int kSmemBytes = kStages * kStageBytes + kBarBytes + 1024;  // + alignment slack
+    static constexpr int kSmemBytes = kStages * kStageBytes + kBarRegion + kCStagingBytes + 1024;  // + alignment slack
+    static_assert(kSmemBytes <= 232448, "over the per-block shared memory limit");
 };
 
 struct KParams {
     int m, n, k;
     int num_m_tiles, num_n_tiles, num_k_blocks, total_tiles;
     void *c;
+    void *c_peers[kMaxPeers];  // the same rows of C in other GPUs' copies (may be empty)
+    int n_peers;
+    int staged;  // 1: C leaves through shared memory and TMA stores (CStoreMaps), 0: direct stores
     long long ldc;
     int c_dtype;
     const void *bias;
@@ -93,58 +105,72 @@ __device__ __forceinline__ float load_bias(const void *bias, int dtype, int i) {
     return __bfloat162float(static_cast<const __nv_bfloat16 *>(bias)[i]);
 }
 
-// Store 32 accumulator columns [col0, col0+32) of one row.
+// Add the bias of columns [col0, col0 + 32) to one accumulator chunk.  Lane
+// l loads the bias of column col0 + l (one coalesced load per warp) and the
+// values reach every lane by shuffle.  Called by all 32 lanes; columns past
+// N get 0 and are never stored.
+__device__ __forceinline__ void add_bias_chunk(const KParams &p, int col0, int lane, uint32_t (&r)[32]) {
+    const int col = col0 + lane;
+    const float mine = col < p.n ? load_bias(p.bias, p.bias_dtype, col) : 0.0f;
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+        r[j] = __float_as_uint(__fadd_rn(__uint_as_float(r[j]), __shfl_sync(0xffffffffu, mine, j)));
+}
+
+// Store 32 accumulator columns [col0, col0+32) of one row (bias already
+// added): conversion once, then the same bytes to this GPU's C and to every
+// peer copy.
 __device__ __forceinline__ void store_row_chunk(const KParams &p, int row, int col0, const uint32_t (&r)[32]) {
     float v[32];
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
     const int cnt = p.n - col0 < 32 ? p.n - col0 : 32;
-    if (p.bias != nullptr) {
-#pragma unroll
-        for (int j = 0; j < 32; ++j)
-            if (j < cnt) v[j] = __fadd_rn(v[j], load_bias(p.bias, p.bias_dtype, col0 + j));
-    }
     const long long off = static_cast<long long>(row) * p.ldc + col0;
     if (p.c_dtype == ST_F32) {
-        float *dst = static_cast<float *>(p.c) + off;
-        if (cnt == 32 && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
+        for (int d = -1; d < p.n_peers; ++d) {
+            float *dst = static_cast<float *>(d < 0 ? p.c : p.c_peers[d]) + off;
+            if (cnt == 32 && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
 #if ST_C_POLICY == 1
-            const uint64_t pol = l2_policy_evict_first();
+                const uint64_t pol = l2_policy_evict_first();
 #pragma unroll
-            for (int j = 0; j < 32; j += 4)
-                asm volatile("st.global.L2::cache_hint.v4.f32 [%0], {%1, %2, %3, %4}, %5;" ::"l"(dst + j),
-                             "f"(v[j]), "f"(v[j + 1]), "f"(v[j + 2]), "f"(v[j + 3]), "l"(pol)
-                             : "memory");
+                for (int j = 0; j < 32; j += 4)
+                    asm volatile("st.global.L2::cache_hint.v4.f32 [%0], {%1, %2, %3, %4}, %5;" ::"l"(dst + j),
+                                 "f"(v[j]), "f"(v[j + 1]), "f"(v[j + 2]), "f"(v[j + 3]), "l"(pol)
+                                 : "memory");
 #else
 #pragma unroll
-            for (int j = 0; j < 32; j += 4)
-                *reinterpret_cast<float4 *>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                for (int j = 0; j < 32; j += 4)
+                    *reinterpret_cast<float4 *>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
 #endif
-        } else {
+            } else {
 #pragma unroll
-            for (int j = 0; j < 32; ++j)
-                if (j < cnt) dst[j] = v[j];
+                for (int j = 0; j < 32; ++j)
+                    if (j < cnt) dst[j] = v[j];
+            }
         }
+        return;
+    }
+    uint16_t h[32];
+    if (p.c_dtype == ST_F16) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) h[j] = __half_as_ushort(__float2half_rn(v[j]));
     } else {
-        uint16_t h[32];
-        if (p.c_dtype == ST_F16) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) h[j] = __half_as_ushort(__float2half_rn(v[j]));
-        } else {
+        for (int j = 0; j < 32; ++j) h[j] = __bfloat16_as_ushort(__float2bfloat16_rn(v[j]));
+    }
+    uint4 q[4];
 #pragma unroll
-            for (int j = 0; j < 32; ++j) h[j] = __bfloat16_as_ushort(__float2bfloat16_rn(v[j]));
-        }
-        uint16_t *dst = static_cast<uint16_t *>(p.c) + off;
+    for (int j = 0; j < 4; ++j) {
+        q[j].x = h[8 * j] | (static_cast<uint32_t>(h[8 * j + 1]) << 16);
+        q[j].y = h[8 * j + 2] | (static_cast<uint32_t>(h[8 * j + 3]) << 16);
+        q[j].z = h[8 * j + 4] | (static_cast<uint32_t>(h[8 * j + 5]) << 16);
+        q[j].w = h[8 * j + 6] | (static_cast<uint32_t>(h[8 * j + 7]) << 16);
+    }
+    for (int d = -1; d < p.n_peers; ++d) {
+        uint16_t *dst = static_cast<uint16_t *>(d < 0 ? p.c : p.c_peers[d]) + off;
         if (cnt == 32 && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
 #pragma unroll
-            for (int j = 0; j < 32; j += 8) {
-                uint4 q;
-                q.x = h[j] | (static_cast<uint32_t>(h[j + 1]) << 16);
-                q.y = h[j + 2] | (static_cast<uint32_t>(h[j + 3]) << 16);
-                q.z = h[j + 4] | (static_cast<uint32_t>(h[j + 5]) << 16);
-                q.w = h[j + 6] | (static_cast<uint32_t>(h[j + 7]) << 16);
-                *reinterpret_cast<uint4 *>(dst + j) = q;
-            }
+            for (int j = 0; j < 4; ++j) reinterpret_cast<uint4 *>(dst)[j] = q[j];
         } else {
 #pragma unroll
             for (int j = 0; j < 32; ++j)
@@ -153,11 +179,87 @@ __device__ __forceinline__ void store_row_chunk(const KParams &p, int row, int c
     }
 }
 
+// Tensor maps of the TMA-store epilogue: [0] this GPU's C, [1 + d] peer copy d.
+// Box = 32 rows x 128 bytes, 128-byte swizzle; extents = this call's C rows x N.
+struct CStoreMaps {
+    CUtensorMap map[1 + kMaxPeers];
+};
+
+// One tile's worth of a warp's 32 accumulator rows (TMEM lanes at t_row,
+// columns [n0, n0 + NCOLS)) through shared memory: bias add and conversion,
+// one 128-byte row per lane written into a swizzled staging box, then one
+// TMA store of the box to C and to every peer copy.  The two staging buffers
+// alternate; before reusing one, lane 0 waits until the store issued from it
+// has finished reading shared memory.  TMA clips the box at C's extents.
+template <int NCOLS>
+__device__ __forceinline__ void store_tile_staged(const KParams &p, const CStoreMaps &cm, uint32_t t_row, int row0,
+                                                  int n0, uint32_t staging, int &buf, int lane) {
+    if (row0 >= p.m) return;
+    const bool f32 = p.c_dtype == ST_F32;
+    const int box_cols = f32 ? 32 : 64;
+#pragma unroll 1
+    for (int c0 = 0; c0 < NCOLS; c0 += box_cols) {
+        const int col0 = n0 + c0;
+        if (col0 >= p.n) break;
+        uint32_t w[32];  // this lane's 128-byte row of the box
+        if (f32) {
+            tmem_load_32(t_row + c0, w);
+            tmem_load_wait();
+            if (p.bias != nullptr) add_bias_chunk(p, col0, lane, w);
+        } else {
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                uint32_t r[32];
+                tmem_load_32(t_row + c0 + 32 * h, r);
+                tmem_load_wait();
+                if (p.bias != nullptr) add_bias_chunk(p, col0 + 32 * h, lane, r);
+#pragma unroll
+                for (int j = 0; j < 32; j += 2) {
+                    const float v0 = __uint_as_float(r[j]), v1 = __uint_as_float(r[j + 1]);
+                    uint32_t lo, hi;
+                    if (p.c_dtype == ST_F16) {
+                        lo = __half_as_ushort(__float2half_rn(v0));
+                        hi = __half_as_ushort(__float2half_rn(v1));
+                    } else {
+                        lo = __bfloat16_as_ushort(__float2bfloat16_rn(v0));
+                        hi = __bfloat16_as_ushort(__float2bfloat16_rn(v1));
+                    }
+                    w[16 * h + j / 2] = lo | (hi << 16);
+                }
+            }
+        }
+        if (lane == 0) bulk_wait_group_read<1>();  // the store that last used this buffer is done reading it
+        __syncwarp();
+        const uint32_t box = staging + static_cast<uint32_t>(buf * kStageBoxBytes);
+        const uint32_t row_addr = box + static_cast<uint32_t>(lane * 128);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            const uint32_t a = row_addr + (static_cast<uint32_t>(q ^ (lane & 7)) << 4);
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(w[4 * q]), "r"(w[4 * q + 1]),
+                         "r"(w[4 * q + 2]), "r"(w[4 * q + 3])
+                         : "memory");
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+            for (int d = 0; d <= p.n_peers; ++d) tma_store_2d(&cm.map[d], box, col0, row0);
+            bulk_commit_group();
+        }
+        buf ^= 1;
+    }
+}
+
+// After a CTA's last peer store: make its NVLink writes visible system-wide
+// before the kernel counts as complete.
+__device__ __forceinline__ void publish_peer_writes(const KParams &p) {
+    if (p.n_peers > 0) __threadfence_system();
+}
+
 // FMT: 0 = f16, 1 = bf16, 2 = tf32.  B_MN: B tiles are N-contiguous.
 template <int FMT, bool B_MN, int BN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                   const KParams p) {
+                   const KParams p, const __grid_constant__ CStoreMaps cmaps) {
     using Cfg = TileCfg<BN>;
     constexpr bool kTf32 = FMT == 2;
     constexpr int kElem = kTf32 ? 4 : 2;
@@ -314,6 +416,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else {
         // ------------------------------------------------ epilogue (warps 2..5)
         const int g = warp & 3;  // TMEM lanes 32g..32g+31 are the ones this warp may read
+        const uint32_t staging = smem_addr(smem + Cfg::kStages * Cfg::kStageBytes + kBarRegion) +
+                                 static_cast<uint32_t>(g * 2 * kStageBoxBytes);
+        int sbuf = 0;
         int iter = 0;
         for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x, ++iter) {
             const int acc = iter & 1;
@@ -331,20 +436,28 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after_sync();
             const int row = m0 + g * 32 + lane;
             const uint32_t t_row = tmem_base + (static_cast<uint32_t>(g * 32) << 16) + static_cast<uint32_t>(acc * BN);
+            if (p.staged) {
+                store_tile_staged<BN>(p, cmaps, t_row, m0 + g * 32, n0, staging, sbuf, lane);
+            } else {
 #pragma unroll 1
-            for (int c = 0; c < BN / 32; ++c) {
-                uint32_t r[32];
-                tmem_load_32(t_row + c * 32, r);
-                tmem_load_wait();
-                const int col0 = n0 + c * 32;
-                if (row < p.m && col0 < p.n) store_row_chunk(p, row, col0, r);
+                for (int c = 0; c < BN / 32; ++c) {
+                    const int col0 = n0 + c * 32;
+                    if (col0 >= p.n) break;
+                    uint32_t r[32];
+                    tmem_load_32(t_row + c * 32, r);
+                    tmem_load_wait();
+                    if (p.bias != nullptr) add_bias_chunk(p, col0, lane, r);
+                    if (row < p.m) store_row_chunk(p, row, col0, r);
+                }
             }
             tc_fence_before_sync();
             __syncwarp();
             if (lane == 0) mbar_arrive(tempty_bar(acc));
         }
+        if (p.staged && lane == 0) bulk_wait_group_all();  // every TMA store of C has landed
     }
 
+    publish_peer_writes(p);
     __syncthreads();
     if (warp == 1) {
         __syncwarp();
@@ -397,13 +510,14 @@ struct PairCfg {
     static constexpr int kStageBytes = kABytes + kBBytes;
     static constexpr int kStages = ST_PAIR_STAGES;
     static constexpr int kTmemCols = 512;  // two 256-column accumulators
-    static constexpr int kSmemBytes = kStages * kStageBytes + 256 + 1024;
+    static constexpr int kSmemBytes = kStages * kStageBytes + kBarRegion + kCStagingBytes + 1024;
+    static_assert(kSmemBytes <= 232448, "over the per-block shared memory limit");
 };
 
 template <int FMT, bool B_MN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                        const KParams p) {
+                        const KParams p, const __grid_constant__ CStoreMaps cmaps) {
     using Cfg = PairCfg;
     constexpr bool kTf32 = FMT == 2;
     constexpr int kElem = kTf32 ? 4 : 2;
@@ -562,6 +676,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     } else {
         // ------------------------------------------------ epilogue (warps 2..5, both CTAs)
         const int g = warp & 3;
+        const uint32_t staging = smem_addr(smem + Cfg::kStages * Cfg::kStageBytes + kBarRegion) +
+                                 static_cast<uint32_t>(g * 2 * kStageBoxBytes);
+        int sbuf = 0;
         const uint32_t even_tempty0 = map_to_rank(tempty_bar(0), 0);
         const uint32_t odd_tfull0 = map_to_rank(tfull_bar(0), 1);
         int iter = 0;
@@ -583,13 +700,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             const int row = m0 + g * 32 + lane;
             const uint32_t t_row =
                 tmem_base + (static_cast<uint32_t>(g * 32) << 16) + static_cast<uint32_t>(acc * kPairN);
+            if (p.staged) {
+                store_tile_staged<kPairN>(p, cmaps, t_row, m0 + g * 32, n0, staging, sbuf, lane);
+            } else {
 #pragma unroll 1
-            for (int c = 0; c < kPairN / 32; ++c) {
-                uint32_t r[32];
-                tmem_load_32(t_row + c * 32, r);
-                tmem_load_wait();
-                const int col0 = n0 + c * 32;
-                if (row < p.m && col0 < p.n) store_row_chunk(p, row, col0, r);
+                for (int c = 0; c < kPairN / 32; ++c) {
+                    const int col0 = n0 + c * 32;
+                    if (col0 >= p.n) break;
+                    uint32_t r[32];
+                    tmem_load_32(t_row + c * 32, r);
+                    tmem_load_wait();
+                    if (p.bias != nullptr) add_bias_chunk(p, col0, lane, r);
+                    if (row < p.m) store_row_chunk(p, row, col0, r);
+                }
             }
             tc_fence_before_sync();
             __syncwarp();
@@ -598,8 +721,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 else mbar_arrive_cluster(even_tempty0 + 8u * acc);
             }
         }
+        if (p.staged && lane == 0) bulk_wait_group_all();  // every TMA store of C has landed
     }
 
+    publish_peer_writes(p);
     tc_fence_before_sync();
     cluster_sync();  // all MMAs retired, all TMEM reads done, no remote access pending
     if (warp == 1) {
@@ -640,10 +765,6 @@ __device__ __forceinline__ uint32_t tf32_bits(float x) {
     if ((u & 0x7f800000u) == 0x7f800000u) return u;
     u += 0x0fffu + ((u >> 13) & 1u);
     return u & 0xffffe000u;
-}
-
-__device__ __forceinline__ void fence_proxy_async_smem() {
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 template <bool B_MN, int BN>
@@ -918,11 +1039,13 @@ __global__ void __launch_bounds__(kX3Threads, 1)
             const uint32_t t_row = tmem_base + (static_cast<uint32_t>(g * 32) << 16) + static_cast<uint32_t>(acc * BN);
 #pragma unroll 1
             for (int c = 0; c < BN / 32; ++c) {
+                const int col0 = n0 + c * 32;
+                if (col0 >= p.n) break;
                 uint32_t r[32];
                 tmem_load_32(t_row + c * 32, r);
                 tmem_load_wait();
-                const int col0 = n0 + c * 32;
-                if (row < p.m && col0 < p.n) store_row_chunk(p, row, col0, r);
+                if (p.bias != nullptr) add_bias_chunk(p, col0, lane, r);
+                if (row < p.m) store_row_chunk(p, row, col0, r);
             }
             tc_fence_before_sync();
             __syncwarp();
@@ -930,6 +1053,7 @@ __global__ void __launch_bounds__(kX3Threads, 1)
         }
     }
 
+    publish_peer_writes(p);
     __syncthreads();
     if (warp == 1) {
         __syncwarp();
@@ -969,7 +1093,8 @@ int make_map(CUtensorMap *map, CUtensorMapDataType dt, const void *base, uint64_
 }
 
 template <int FMT, bool B_MN, int BN>
-int launch_instance(const CUtensorMap &ma, const CUtensorMap &mb, const KParams &kp, int ctas, cudaStream_t stream) {
+int launch_instance(const CUtensorMap &ma, const CUtensorMap &mb, const KParams &kp, const CStoreMaps &cm, int ctas,
+                    cudaStream_t stream) {
     using Cfg = TileCfg<BN>;
     auto kern = gemm_tc_kernel<FMT, B_MN, BN>;
     static uint64_t attr_set = 0;  // one bit per device ordinal
@@ -979,26 +1104,26 @@ int launch_instance(const CUtensorMap &ma, const CUtensorMap &mb, const KParams 
         ST_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
         if (dev >= 0 && dev < 64) attr_set |= 1ull << dev;
     }
-    kern<<<ctas, kThreads, Cfg::kSmemBytes, stream>>>(ma, mb, kp);
+    kern<<<ctas, kThreads, Cfg::kSmemBytes, stream>>>(ma, mb, kp, cm);
     note_launch();
     const cudaError_t e = cudaPeekAtLastError();
     return e == cudaSuccess ? ST_OK : cuda_fail(cudaGetLastError(), "gemm_tc_kernel launch");
 }
 
 template <int FMT, bool B_MN>
-int dispatch_bn(int bn, const CUtensorMap &ma, const CUtensorMap &mb, const KParams &kp, int ctas,
-                cudaStream_t stream) {
+int dispatch_bn(int bn, const CUtensorMap &ma, const CUtensorMap &mb, const KParams &kp, const CStoreMaps &cm,
+                int ctas, cudaStream_t stream) {
     switch (bn) {
-    case 256: return launch_instance<FMT, B_MN, 256>(ma, mb, kp, ctas, stream);
-    case 128: return launch_instance<FMT, B_MN, 128>(ma, mb, kp, ctas, stream);
-    case 64: return launch_instance<FMT, B_MN, 64>(ma, mb, kp, ctas, stream);
+    case 256: return launch_instance<FMT, B_MN, 256>(ma, mb, kp, cm, ctas, stream);
+    case 128: return launch_instance<FMT, B_MN, 128>(ma, mb, kp, cm, ctas, stream);
+    case 64: return launch_instance<FMT, B_MN, 64>(ma, mb, kp, cm, ctas, stream);
     default: return fail(ST_ERR_UNSUPPORTED, "unsupported block_n");
     }
 }
 
 template <int FMT, bool B_MN>
-int launch_pair(const CUtensorMap &ma, const CUtensorMap &mb, const KParams &kp, int pairs_wanted,
-                cudaStream_t stream) {
+int launch_pair(const CUtensorMap &ma, const CUtensorMap &mb, const KParams &kp, const CStoreMaps &cm,
+                int pairs_wanted, cudaStream_t stream) {
     auto kern = gemm_tc_pair_kernel<FMT, B_MN>;
     static uint64_t attr_set = 0;
     static int max_clusters[64] = {0};
@@ -1032,7 +1157,7 @@ int launch_pair(const CUtensorMap &ma, const CUtensorMap &mb, const KParams &kp,
     if (std::getenv("SPTILES_B200_DEBUG"))
         std::fprintf(stderr, "[sptiles_b200] pair gemm: %d pairs (wanted %d, co-resident clusters %d), smem %d\n",
                      pairs, pairs_wanted, clusters, PairCfg::kSmemBytes);
-    kern<<<2 * pairs, kThreads, PairCfg::kSmemBytes, stream>>>(ma, mb, kp);
+    kern<<<2 * pairs, kThreads, PairCfg::kSmemBytes, stream>>>(ma, mb, kp, cm);
     note_launch();
     const cudaError_t e = cudaPeekAtLastError();
     return e == cudaSuccess ? ST_OK : cuda_fail(cudaGetLastError(), "gemm_tc_pair_kernel launch");
@@ -1116,6 +1241,9 @@ int launch_gemm_3xtf32(const GemmArgs &g, int sm_count, int *dev_err, uint64_t t
     kp.num_k_blocks = static_cast<int>(cdiv(g.k, 32));
     kp.total_tiles = kp.num_m_tiles * kp.num_n_tiles;
     kp.c = g.c;
+    kp.staged = 0;  // direct stores
+    kp.n_peers = g.peers.n;
+    for (int i = 0; i < kMaxPeers; ++i) kp.c_peers[i] = i < g.peers.n ? g.peers.base[i] : nullptr;
     kp.ldc = g.ldc;
     kp.c_dtype = g.c_dtype;
     kp.bias = g.bias;
@@ -1188,6 +1316,27 @@ int plan_gemm(int in_dtype, int64_t m, int64_t n, int64_t k, int sm_count, GemmP
     return ST_OK;
 }
 
+// The TMA-store epilogue needs every C destination 16-byte aligned with a
+// row stride of a multiple of 16 bytes; other C views take the per-lane
+// direct stores.  Peer copies always go by TMA store (one asynchronous bulk
+// store per box and destination instead of per-lane stores across NVLink);
+// a local C does unless SPTILES_B200_C_STORE=direct (or =tma) overrides it.
+bool c_store_staged(const GemmArgs &g) {
+    const int ces = dtype_size(g.c_dtype);
+    if ((g.ldc * ces) % 16 != 0) return false;
+    if (reinterpret_cast<uintptr_t>(g.c) % 16 != 0) return false;
+    for (int d = 0; d < g.peers.n; ++d)
+        if (reinterpret_cast<uintptr_t>(g.peers.base[d]) % 16 != 0) return false;
+    if (g.peers.n > 0) return true;
+    static const int mode = [] {
+        const char *v = std::getenv("SPTILES_B200_C_STORE");
+        if (v != nullptr && std::strcmp(v, "direct") == 0) return 0;
+        if (v != nullptr && std::strcmp(v, "tma") == 0) return 1;
+        return ST_C_STORE_DEFAULT;
+    }();
+    return mode != 0;
+}
+
 int launch_gemm(const GemmArgs &g, int sm_count, int *dev_err, uint64_t timeout_ns, cudaStream_t stream) {
     GemmPlan plan;
     // the packed tf32 K already includes the 3x expansion; plan on the product extents
@@ -1223,31 +1372,46 @@ int launch_gemm(const GemmArgs &g, int sm_count, int *dev_err, uint64_t timeout_
     kp.num_k_blocks = static_cast<int>(cdiv(g.k, bk));
     kp.total_tiles = kp.num_m_tiles * kp.num_n_tiles;
     kp.c = g.c;
+    kp.n_peers = g.peers.n;
+    for (int i = 0; i < kMaxPeers; ++i) kp.c_peers[i] = i < g.peers.n ? g.peers.base[i] : nullptr;
     kp.ldc = g.ldc;
     kp.c_dtype = g.c_dtype;
     kp.bias = g.bias;
     kp.bias_dtype = g.bias_dtype;
     kp.err = dev_err;
     kp.timeout_ns = timeout_ns;
+    CStoreMaps cm;
+    std::memset(&cm, 0, sizeof(cm));
+    kp.staged = 0;
+    if (c_store_staged(g)) {
+        const CUtensorMapDataType cdt = g.c_dtype == ST_F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                                            : (g.c_dtype == ST_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                                                   : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16);
+        const int ces = dtype_size(g.c_dtype);
+        for (int d = 0; d <= g.peers.n; ++d)
+            ST_TRY(make_map(&cm.map[d], cdt, d == 0 ? g.c : g.peers.base[d - 1], static_cast<uint64_t>(g.n),
+                            static_cast<uint64_t>(g.m), static_cast<uint64_t>(g.ldc) * ces, 128 / ces, 32));
+        kp.staged = 1;
+    }
     if (plan.pair) {
         const int pairs = plan.ctas / 2;
         if (g.ab_dtype == ST_F16)
-            return g.b_k_major ? launch_pair<0, false>(ma, mb, kp, pairs, stream)
-                               : launch_pair<0, true>(ma, mb, kp, pairs, stream);
+            return g.b_k_major ? launch_pair<0, false>(ma, mb, kp, cm, pairs, stream)
+                               : launch_pair<0, true>(ma, mb, kp, cm, pairs, stream);
         if (g.ab_dtype == ST_BF16)
-            return g.b_k_major ? launch_pair<1, false>(ma, mb, kp, pairs, stream)
-                               : launch_pair<1, true>(ma, mb, kp, pairs, stream);
-        return launch_pair<2, false>(ma, mb, kp, pairs, stream);
+            return g.b_k_major ? launch_pair<1, false>(ma, mb, kp, cm, pairs, stream)
+                               : launch_pair<1, true>(ma, mb, kp, cm, pairs, stream);
+        return launch_pair<2, false>(ma, mb, kp, cm, pairs, stream);
     }
     if (g.ab_dtype == ST_F16) {
-        return g.b_k_major ? dispatch_bn<0, false>(plan.block_n, ma, mb, kp, plan.ctas, stream)
-                           : dispatch_bn<0, true>(plan.block_n, ma, mb, kp, plan.ctas, stream);
+        return g.b_k_major ? dispatch_bn<0, false>(plan.block_n, ma, mb, kp, cm, plan.ctas, stream)
+                           : dispatch_bn<0, true>(plan.block_n, ma, mb, kp, cm, plan.ctas, stream);
     }
     if (g.ab_dtype == ST_BF16) {
-        return g.b_k_major ? dispatch_bn<1, false>(plan.block_n, ma, mb, kp, plan.ctas, stream)
-                           : dispatch_bn<1, true>(plan.block_n, ma, mb, kp, plan.ctas, stream);
+        return g.b_k_major ? dispatch_bn<1, false>(plan.block_n, ma, mb, kp, cm, plan.ctas, stream)
+                           : dispatch_bn<1, true>(plan.block_n, ma, mb, kp, cm, plan.ctas, stream);
     }
-    return dispatch_bn<2, false>(plan.block_n, ma, mb, kp, plan.ctas, stream);
+    return dispatch_bn<2, false>(plan.block_n, ma, mb, kp, cm, plan.ctas, stream);
 }
 
 }  // namespace st

@@ -308,18 +308,20 @@ __global__ void fill_rows_kernel(void *c, int64_t ldc, int c_dtype, const void *
 }
 
 int matmul_device(const ExecCtx &x, const st_tensor &a, const st_tensor &b, const st_tensor *bias,
-                  const st_tensor &c) {
+                  const st_tensor &c, const PeerOutputs *peers = nullptr) {
     const int64_t M = a.shape[0], K = a.shape[1], N = b.shape[1];
     if (M == 0 || N == 0) return ST_OK;
     const void *bias_ptr = bias ? bias->data : nullptr;
     const int bias_dtype = bias ? bias->dtype : ST_F32;
     if (K == 0) {  // empty contraction: C = 0 (+ bias)
+        if (peers && peers->n > 0) return fail(ST_ERR_UNSUPPORTED, "K = 0 with peer outputs");
         fill_rows_kernel<<<148, 256, 0, x.stream>>>(c.data, c.strides[0], c.dtype, bias_ptr, bias_dtype, M, N);
         note_launch();
         const cudaError_t e = cudaPeekAtLastError();
         return e == cudaSuccess ? ST_OK : cuda_fail(cudaGetLastError(), "fill_rows_kernel");
     }
     GemmArgs g{};
+    if (peers) g.peers = *peers;
     g.c = c.data;
     g.ldc = c.strides[0];
     g.c_dtype = c.dtype;
@@ -1142,6 +1144,66 @@ int st_matmul_host(st_ctx *ctx, const st_tensor *a, const st_tensor *b, const st
     ST_TRY(stage_out(x, dc, *c));
     ST_TRY(ws_release(x.dev->stage, x.stream));
     return bounded_sync(x.dev, x.stream, x.timeout_ms);
+}
+
+int st_ipc_handle(st_ctx *ctx, int32_t device, void *ptr, uint8_t handle[64]) {
+    DeviceState *d;
+    ST_TRY(get_dev(ctx, device, &d));
+    if (!ptr || !handle) return fail(ST_ERR_INVALID_ARGUMENT, "st_ipc_handle: null pointer");
+    static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+    DeviceGuard guard(d->ordinal);
+    cudaIpcMemHandle_t h;
+    ST_CUDA_TRY(cudaIpcGetMemHandle(&h, ptr));
+    std::memcpy(handle, &h, 64);
+    return ST_OK;
+}
+
+int st_ipc_open(st_ctx *ctx, int32_t device, const uint8_t handle[64], void **out) {
+    DeviceState *d;
+    ST_TRY(get_dev(ctx, device, &d));
+    if (!handle || !out) return fail(ST_ERR_INVALID_ARGUMENT, "st_ipc_open: null pointer");
+    DeviceGuard guard(d->ordinal);
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, 64);
+    ST_CUDA_TRY(cudaIpcOpenMemHandle(out, h, cudaIpcMemLazyEnablePeerAccess));
+    return ST_OK;
+}
+
+int st_ipc_close(st_ctx *ctx, int32_t device, void *ptr) {
+    DeviceState *d;
+    ST_TRY(get_dev(ctx, device, &d));
+    DeviceGuard guard(d->ordinal);
+    if (ptr) ST_CUDA_TRY(cudaIpcCloseMemHandle(ptr));
+    return ST_OK;
+}
+
+int st_matmul_allgather(st_ctx *ctx, const st_tensor *a, const st_tensor *b, const st_tensor *bias,
+                        const st_tensor *c_full, void *const *peer_c_full, int32_t n_peers, int64_t row_offset,
+                        const st_exec *exec) {
+    ExecCtx x;
+    ST_TRY(resolve_exec(ctx, exec, &x));
+    if (!a || !c_full) return fail(ST_ERR_INVALID_ARGUMENT, "st_matmul_allgather: null tensor");
+    ST_TRY(check_view(c_full, "C", 2));
+    if (n_peers < 0 || n_peers > kMaxPeers || (n_peers > 0 && !peer_c_full))
+        return fail(ST_ERR_INVALID_ARGUMENT, "st_matmul_allgather: between 0 and 7 peer copies of C");
+    if (row_offset < 0 || a->rank != 2 || row_offset + a->shape[0] > c_full->shape[0])
+        return fail(ST_ERR_INVALID_ARGUMENT, "st_matmul_allgather: A's rows must fall inside C at row_offset");
+    // this rank's rows of C, and the same rows in each peer's copy
+    const size_t es = dtype_size(c_full->dtype);
+    const size_t byte_off = static_cast<size_t>(row_offset) * static_cast<size_t>(c_full->strides[0]) * es;
+    st_tensor c_rows = *c_full;
+    c_rows.shape[0] = a->shape[0];
+    c_rows.data = static_cast<uint8_t *>(c_full->data) + byte_off;
+    ST_TRY(check_matmul(a, b, bias, &c_rows));
+    PeerOutputs peers;
+    peers.n = n_peers;
+    for (int i = 0; i < n_peers; ++i) {
+        if (!peer_c_full[i]) return fail(ST_ERR_INVALID_ARGUMENT, "st_matmul_allgather: null peer pointer");
+        peers.base[i] = static_cast<uint8_t *>(peer_c_full[i]) + byte_off;
+    }
+    DeviceGuard guard(x.dev->ordinal);
+    ST_TRY(matmul_device(x, *a, *b, bias, c_rows, &peers));
+    return finish(x);
 }
 
 int st_shard_range(int64_t total, int32_t count, int32_t rank, int64_t align, int64_t *begin, int64_t *end) {

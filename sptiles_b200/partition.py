@@ -37,12 +37,14 @@ def matmul_row_shard(m: int, world_size: int, rank: int) -> tuple[int, int]:
     return shard_range(m, world_size, rank, MATMUL_ROW_ALIGN)
 
 
-def gather_row_shards(local: torch.Tensor, m_total: int, *, group=None) -> torch.Tensor:
+def gather_row_shards(local: torch.Tensor, m_total: int, *, group=None, out: torch.Tensor | None = None
+                      ) -> torch.Tensor:
     """All-gather the row blocks of a row-sharded [m_total, N] matrix.
 
-    ``local`` holds this rank's rows (``matmul_row_shard``).  Shards may
-    differ in size, so each is padded to the largest before one
-    all_gather_into_tensor, and the padding is dropped afterwards.
+    ``local`` holds this rank's rows (``matmul_row_shard``).  Equal shards
+    gather straight into ``out`` (allocated if not given) with one
+    all_gather_into_tensor; unequal shards are padded to the largest first
+    and the padding is dropped afterwards.
     """
     rank = dist.get_rank(group)
     ws = dist.get_world_size(group)
@@ -53,14 +55,19 @@ def gather_row_shards(local: torch.Tensor, m_total: int, *, group=None) -> torch
     n = local.shape[1]
     mx = max(rows)
     if all(r == mx for r in rows):
-        out = torch.empty((m_total, n), dtype=local.dtype, device=local.device)
+        if out is None:
+            out = torch.empty((m_total, n), dtype=local.dtype, device=local.device)
         dist.all_gather_into_tensor(out, local.contiguous(), group=group)
         return out
     padded = torch.zeros((mx, n), dtype=local.dtype, device=local.device)
     padded[: local.shape[0]] = local
     buf = torch.empty((ws * mx, n), dtype=local.dtype, device=local.device)
     dist.all_gather_into_tensor(buf, padded, group=group)
-    return torch.cat([buf[r * mx: r * mx + rows[r]] for r in range(ws)], dim=0)
+    full = torch.cat([buf[r * mx: r * mx + rows[r]] for r in range(ws)], dim=0)
+    if out is not None:
+        out.copy_(full)
+        return out
+    return full
 
 
 def sharded_matmul(a_local: torch.Tensor, b: torch.Tensor, bias: torch.Tensor | None = None, *, m_total: int,
@@ -79,3 +86,105 @@ def sharded_vector_add(a_local: torch.Tensor, b_local: torch.Tensor) -> torch.Te
     from .api import vector_add
 
     return vector_add(a_local, b_local)
+
+
+class _DeviceArray:
+    """A raw device allocation presented to torch (no ownership)."""
+
+    def __init__(self, ptr: int, shape: tuple[int, ...], typestr: str):
+        self.__cuda_array_interface__ = {"data": (ptr, False), "shape": shape, "typestr": typestr,
+                                         "strides": None, "version": 3}
+
+
+class ReplicatedOutput:
+    """An [M, N] C held on every rank, with every rank's copy mapped into the others.
+
+    The replicated-output mode of the partitioner with the all-gather fused
+    into the GEMM: each rank allocates its copy (``st_alloc``), exports it
+    (``st_ipc_handle``), the handles are exchanged over the process group, and
+    each rank maps the other copies (``st_ipc_open``, NVLink peer memory on
+    the B200 box).  :meth:`matmul` computes this rank's row block and the
+    kernel's epilogue stores every finished chunk into all copies; one-
+    element all-reduces on the current stream order the kernel after earlier
+    work on every rank and later work on each rank after every rank's kernel.
+    Call :meth:`close` on all ranks when done.
+    """
+
+    def __init__(self, m: int, n: int, dtype: torch.dtype, *, group=None):
+        import ctypes
+
+        from . import _native as N
+        from .api import dtype_code
+        from .runtime import context
+
+        self.m, self.n, self.dtype, self.group = m, n, dtype, group
+        self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
+        if self.world - 1 > 7:
+            raise ValueError("at most 8 ranks share one replicated output")
+        self.device = torch.cuda.current_device()
+        self._ctx = context(self.device)
+        self._N = N
+        dtype_code(dtype)  # validates the type
+        esize = torch.empty((), dtype=dtype).element_size()
+        ptr = ctypes.c_void_p()
+        N.check(N.lib().st_alloc(self._ctx, self.device, m * n * esize, ctypes.byref(ptr)), "st_alloc")
+        self._ptr = ptr.value
+        handle = (ctypes.c_uint8 * 64)()
+        N.check(N.lib().st_ipc_handle(self._ctx, self.device, self._ptr, handle), "st_ipc_handle")
+        handles: list = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self._peers = []
+        for r, h in enumerate(handles):
+            if r == self.rank:
+                continue
+            p = ctypes.c_void_p()
+            N.check(N.lib().st_ipc_open(self._ctx, self.device, (ctypes.c_uint8 * 64)(*h), ctypes.byref(p)),
+                    f"st_ipc_open(rank {r})")
+            self._peers.append(p.value)
+        typestr = {4: "<f4", 2: "<f2"}[esize]
+        t = torch.as_tensor(_DeviceArray(self._ptr, (m, n), typestr), device=f"cuda:{self.device}")
+        self.tensor = t.view(dtype) if t.dtype != dtype else t
+        self._flag = torch.zeros(1, device=f"cuda:{self.device}")
+        self._peer_array = (ctypes.c_void_p * max(1, len(self._peers)))(*self._peers)
+        self.rows = matmul_row_shard(m, self.world, self.rank)
+
+    def matmul(self, a_local: torch.Tensor, b: torch.Tensor, bias: torch.Tensor | None = None, *,
+               wait_for_readers: bool = True) -> torch.Tensor:
+        """C = A @ B (+ bias) replicated on every rank; ``a_local`` holds this rank's rows.
+
+        The kernel writes into the other ranks' copies, so by default a one-
+        element all-reduce first orders it after all work already queued on
+        every rank (readers of the previous result included).  Pass
+        ``wait_for_readers=False`` only when nothing reads the copies between
+        two calls.
+        """
+        import ctypes
+
+        from .api import _exec_for, tensor_view
+
+        r0, r1 = self.rows
+        if a_local.shape[0] != r1 - r0:
+            raise ValueError(f"rank {self.rank} holds {a_local.shape[0]} rows, its shard has {r1 - r0}")
+        if wait_for_readers:
+            dist.all_reduce(self._flag, group=self.group)
+        ex = _exec_for(a_local)
+        va, vb, vc = tensor_view(a_local), tensor_view(b), tensor_view(self.tensor)
+        vbias = ctypes.byref(tensor_view(bias)) if bias is not None else None
+        self._N.check(self._N.lib().st_matmul_allgather(self._ctx, ctypes.byref(va), ctypes.byref(vb), vbias,
+                                                        ctypes.byref(vc), self._peer_array, len(self._peers), r0,
+                                                        ctypes.byref(ex)), "st_matmul_allgather")
+        # every rank's kernel (and so every write into this copy) precedes this
+        dist.all_reduce(self._flag, group=self.group)
+        return self.tensor
+
+    def close(self) -> None:
+        if self._ptr is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)  # no rank still writes into a copy
+        for p in self._peers:
+            self._N.lib().st_ipc_close(self._ctx, self.device, p)
+        dist.barrier(group=self.group)  # nobody maps this copy any more
+        self._N.lib().st_free(self._ctx, self.device, self._ptr)
+        self._ptr = None
+        self._peers = []
