@@ -67,6 +67,7 @@ def parse_args():
                         "C chunk into every rank's copy over NVLink peer memory; nccl: the GEMM, then an NCCL "
                         "all-gather of the row blocks")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-sweep", action="store_true", help="vector_add_1d: skip the N = 2^20 .. 2^28 sweep")
     p.add_argument("--timing", choices=["auto", "graph", "eager"], default="auto",
                    help="graph: replay the K timed steps from one CUDA graph (host launch overhead out of the "
                         "timed region); eager: launch every step from the host; auto: graph for the "
@@ -382,6 +383,33 @@ def e2e_matmul(wl, args, a, b, bias, out_dt, rows, dist_on):
                    "host wall clock"}
 
 
+def vector_add_sweep(dev, peaks, exps=(20, 22, 24, 26, 28)):
+    """1D add at N = 2^20 .. 2^28 fp32: HBM GB/s (12 bytes per element) and
+    its fraction of the measured copy bandwidth.  Steps rotate through buffer
+    sets totalling > 2x L2 (one set from 2^24 up: 201 MB and more), ~50 ms of
+    graph-replayed steps per size after 3 warm-up steps."""
+    import torch
+    import sptiles_b200 as st
+    rows = []
+    for e in exps:
+        n = 2 ** e
+        sets = min(64, max(1, math.ceil(2 * L2_BYTES / (12 * n))))
+        bufs = [(torch.rand(n, device=dev) * 2 - 1, torch.rand(n, device=dev) * 2 - 1, torch.empty(n, device=dev))
+                for _ in range(sets)]
+        steps = int(min(2000, max(20, 0.05 / (12 * n / (peaks["hbm_gbs"] * 1e9)))))
+
+        def step(i, bufs=bufs, sets=sets):
+            a, b, c = bufs[i % sets]
+            st.vector_add(a, b, out=c)
+        ms, _ = time_steps(step, steps, 3, torch.cuda.current_stream(dev), False, graph=True)
+        gbs = 12 * n * steps / (ms / 1e3) / 1e9
+        rows.append({"n": n, "GBps": round(gbs, 1), "frac": round(gbs / peaks["hbm_gbs"], 4), "steps": steps,
+                     "buffer_sets": sets, "us_per_launch": round(ms / steps * 1e3, 2)})
+        del bufs
+        torch.cuda.empty_cache()
+    return rows
+
+
 def run_vector_add(wl, args, rank, world, local, dist_on, peaks):
     import torch
     import sptiles_b200 as st
@@ -425,6 +453,10 @@ def run_vector_add(wl, args, rank, world, local, dist_on, peaks):
             "ms_per_launch": round(ms / args.steps, 5)}
     out = dict(value=value, ms_per_step=ms_max / args.steps, roofline=roof, gpu_launches=int(launches),
                clocks=clk.summary(), sets=sets, elements=n)
+    if len(wl["shape"]) == 1 and world == 1 and not args.no_sweep:
+        del bufs
+        out["sweep_1d"] = vector_add_sweep(dev, peaks)
+        bufs = [(torch.rand(n, device=dev), torch.rand(n, device=dev), torch.empty(n, device=dev))]
     if not args.no_e2e:
         a, b, c = bufs[0]
         ha, hb = a.cpu().pin_memory(), b.cpu().pin_memory()
@@ -638,6 +670,8 @@ def main():
                     line["allgather"] = res.get("allgather")
             if secondary:
                 line["vecadd"] = secondary
+            if res.get("sweep_1d"):
+                line["sweep_1d"] = res["sweep_1d"]
             print(json.dumps(line), flush=True)
     finally:
         if dist_on:

@@ -228,6 +228,15 @@ int st_tile_raster(int64_t m, int64_t n, int64_t tm, int64_t tn, int64_t group_m
 int st_matmul_plan(int32_t in_dtype, int64_t m, int64_t n, int64_t k, int32_t sm_count,
                    int32_t *block_m, int32_t *block_n, int32_t *block_k, int32_t *stages,
                    int32_t *ctas);
+/* Work split of the CTA-pair matmul kernel for `tiles` 256 x 256 output
+ * tiles of `k_blocks` K blocks each on `pairs` CTA pairs: tiles
+ * [0, dp_tiles) go out whole (tile t to pair t mod pairs); the remaining
+ * tiles' K blocks (sk_iters of them) are split into sk_pairs equal
+ * contiguous ranges, range q = [q * sk_iters / sk_pairs, (q + 1) * sk_iters
+ * / sk_pairs) on pair pairs - 1 - q (sk_pairs = 0: whole tiles only).  No
+ * counterpart in the reference. */
+int st_stream_k_split(int32_t tiles, int32_t pairs, int32_t k_blocks, int32_t *dp_tiles, int32_t *sk_pairs,
+                      int64_t *sk_iters);
 /* Contiguous shard [begin, end) of `total` units for `rank` of `count`
  * ranks, boundaries rounded to multiples of `align` units (vector_add: 4
  * elements = 16 bytes; matmul: M rows). */

@@ -14,7 +14,7 @@ from .api import (  # noqa: F401
 from .runtime import (  # noqa: F401
     LOCAL_SIZE_X, ceil_div, context, device_count, grid_from_dispatch, kernel_launches, matmul_plan,
     run_tile_kernel,
-    shard_range, shutdown, sync, tensor_1d_descriptor, tensor_2d_descriptor, tile_raster,
+    shard_range, shutdown, stream_k_split, sync, tensor_1d_descriptor, tensor_2d_descriptor, tile_raster,
 )
 from ._native import DeviceAbort, NativeError, lib  # noqa: F401
 

@@ -33,7 +33,7 @@ EXPORTED = (
     "st_version", "st_last_error", "st_device_count", "st_kernel_launches", "st_init", "st_shutdown", "st_sync", "st_stream",
     "st_alloc", "st_free", "st_upload", "st_download", "st_launch", "st_grid_from_dispatch",
     "st_vector_add", "st_matmul", "st_vector_add_host", "st_matmul_host", "st_tile_raster",
-    "st_matmul_plan", "st_shard_range", "st_matmul_static_scratch", "st_vector_fma", "st_cast",
+    "st_matmul_plan", "st_stream_k_split", "st_shard_range", "st_matmul_static_scratch", "st_vector_fma", "st_cast",
     "st_ipc_handle", "st_ipc_open", "st_ipc_close", "st_matmul_allgather",
 )
 
@@ -107,6 +107,7 @@ def _declare(L: ctypes.CDLL) -> None:
                                  _P(StExec)], _c.c_int),
         "st_tile_raster": ([i64, i64, i64, i64, i64, i64, _P(i64), _P(i64)], _c.c_int),
         "st_matmul_plan": ([i32, i64, i64, i64, i32, _P(i32), _P(i32), _P(i32), _P(i32), _P(i32)], _c.c_int),
+        "st_stream_k_split": ([i32, i32, i32, _P(i32), _P(i32), _P(i64)], _c.c_int),
         "st_shard_range": ([i64, i32, i32, i64, _P(i64), _P(i64)], _c.c_int),
         "st_matmul_static_scratch": ([_P(StTensor), _P(StTensor), _P(StTensor), _P(StTensor), _P(StExec)],
                                      _c.c_int),

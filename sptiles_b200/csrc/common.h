@@ -48,6 +48,7 @@ inline size_t dtype_size(int dtype) {
 constexpr int kDevAbortGemmProducer = 0x101;
 constexpr int kDevAbortGemmMma = 0x102;
 constexpr int kDevAbortGemmEpilogue = 0x103;
+constexpr int kDevAbortGemmStreamK = 0x104;  // a split tile's partial never arrived
 
 // ---- launchers (implemented in vecadd.cu, gemm.cu, pack.cu) ----
 
@@ -107,7 +108,15 @@ struct GemmArgs {
     const void *bias;
     int bias_dtype;
     int64_t m, n, k;
+    // stream-K tail of the CTA-pair kernel (null: whole tiles only); sized by
+    // stream_k_workspace_bytes, flags zero when idle
+    float *sk_ws = nullptr;
+    int *sk_flags = nullptr;
 };
+// Partial accumulators (one 256 x 256 fp32 tile per CTA pair) and arrival
+// flags of the stream-K tail, for up to sm_count / 2 pairs.
+size_t stream_k_workspace_bytes(int sm_count);
+size_t stream_k_flag_offset(int sm_count);
 int launch_gemm(const GemmArgs &args, int sm_count, int *dev_err, uint64_t timeout_ns, cudaStream_t stream);
 // fp32 A and B used in place (TMA-addressable): the split into tf32 hi/lo
 // happens in shared memory inside the kernel (args.ab_dtype must be ST_F32,

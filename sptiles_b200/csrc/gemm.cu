@@ -87,6 +87,8 @@ struct TileCfg {
 struct KParams {
     int m, n, k;
     int num_m_tiles, num_n_tiles, num_k_blocks, total_tiles;
+    float *sk_ws;    // stream-K partials (CTA-pair kernel); null: whole tiles only
+    int *sk_flags;   // per (pair, CTA, epilogue warp): partials stored and not yet folded
     void *c;
     void *c_peers[kMaxPeers];  // the same rows of C in other GPUs' copies (may be empty)
     int n_peers;
@@ -185,6 +187,31 @@ struct CStoreMaps {
     CUtensorMap map[1 + kMaxPeers];
 };
 
+// One 128-byte row per lane of a 32-row staging box in the 128-byte swizzle
+// (16-byte chunk j of row l at j ^ (l mod 8): conflict-free for a warp).
+__device__ __forceinline__ void box_put_row(uint32_t box, int lane, const uint32_t (&w)[32]) {
+    const uint32_t row_addr = box + static_cast<uint32_t>(lane * 128);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+        const uint32_t a = row_addr + (static_cast<uint32_t>(q ^ (lane & 7)) << 4);
+        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(w[4 * q]), "r"(w[4 * q + 1]),
+                     "r"(w[4 * q + 2]), "r"(w[4 * q + 3])
+                     : "memory");
+    }
+}
+
+__device__ __forceinline__ void box_get_row(uint32_t box, int lane, uint32_t (&w)[32]) {
+    const uint32_t row_addr = box + static_cast<uint32_t>(lane * 128);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+        const uint32_t a = row_addr + (static_cast<uint32_t>(q ^ (lane & 7)) << 4);
+        asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                     : "=r"(w[4 * q]), "=r"(w[4 * q + 1]), "=r"(w[4 * q + 2]), "=r"(w[4 * q + 3])
+                     : "r"(a)
+                     : "memory");
+    }
+}
+
 // One tile's worth of a warp's 32 accumulator rows (TMEM lanes at t_row,
 // columns [n0, n0 + NCOLS)) through shared memory: bias add and conversion,
 // one 128-byte row per lane written into a swizzled staging box, then one
@@ -231,14 +258,7 @@ __device__ __forceinline__ void store_tile_staged(const KParams &p, const CStore
         if (lane == 0) bulk_wait_group_read<1>();  // the store that last used this buffer is done reading it
         __syncwarp();
         const uint32_t box = staging + static_cast<uint32_t>(buf * kStageBoxBytes);
-        const uint32_t row_addr = box + static_cast<uint32_t>(lane * 128);
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-            const uint32_t a = row_addr + (static_cast<uint32_t>(q ^ (lane & 7)) << 4);
-            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(w[4 * q]), "r"(w[4 * q + 1]),
-                         "r"(w[4 * q + 2]), "r"(w[4 * q + 3])
-                         : "memory");
-        }
+        box_put_row(box, lane, w);
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
@@ -504,6 +524,219 @@ __device__ __forceinline__ uint64_t operand_l2_policy() {
 #endif
 }
 
+// ---- work of one CTA pair: whole tiles, then a stream-K tail
+//
+// With T tiles, P pairs and KB K blocks per tile, tiles go out whole in the
+// strided order (tile t to pair t mod P), which keeps the pairs on
+// neighbouring tiles of the raster for L2 reuse.  With fewer tiles than pairs
+// (T < P) that would leave P - T pairs idle; instead the T * KB K blocks are
+// split into equal contiguous ranges over S > T pairs (at least KB / 4 blocks
+// each, so a tile has at most ~5 pieces).  The split is written for a tail
+// after whole-tile waves too (dp_tiles > 0), but measured no faster there.  The pair whose range holds a split tile's first K block owns the
+// tile: it adds the other pieces' fp32 partials to its accumulator and runs
+// the epilogue.  The other pieces come first in their pairs' ranges (a range
+// starts inside the tile), so their partials are long stored when the owner,
+// which reaches the tile at the end of its range, needs them.  Stream-K
+// index q = P - 1 - pair: a contributor has a lower pair number than its
+// owner, and nothing a contributor does waits on an owner.
+enum : int { kUnitWhole = 0, kUnitOwner = 1, kUnitPiece = 2 };
+
+struct PairWork {
+    int tile, k0, k1, kind;
+};
+
+__host__ __device__ __forceinline__ void stream_k_split(int total, int num_pairs, int kb, bool enabled, int &dp_tiles,
+                                                        int &sk_pairs, long long &sk_iters) {
+    dp_tiles = total;
+    sk_pairs = 0;
+    sk_iters = 0;
+    // only with fewer tiles than pairs: with a whole tile for every pair first,
+    // the balanced tail's fold and extra stores cost what the idle pairs of a
+    // whole-tile tail do (B200, 8192 x 8192 K, 1024 and 2048 rows: -3 % / +1 %)
+    if (!enabled || num_pairs <= 0 || total >= num_pairs || total == 0 || kb < 8) return;
+    const int r = total;
+    const long long iters = static_cast<long long>(r) * kb;
+    const long long per = kb / 4 > 4 ? kb / 4 : 4;
+    long long s = iters / per;
+    if (s > num_pairs) s = num_pairs;
+    if (s <= r) return;  // no better than one whole tile on each of r pairs
+    dp_tiles = total - r;
+    sk_pairs = static_cast<int>(s);
+    sk_iters = iters;
+}
+
+struct PairSchedule {
+    int num_pairs, kb, dp_tiles, sk_pairs, sk_index;
+    long long sk_iters;
+    __device__ __forceinline__ void init(const KParams &p, int pair, int num_pairs_, int total) {
+        num_pairs = num_pairs_;
+        kb = p.num_k_blocks;
+        stream_k_split(total, num_pairs, kb, p.sk_ws != nullptr, dp_tiles, sk_pairs, sk_iters);
+        sk_index = num_pairs - 1 - pair;
+    }
+    __device__ __forceinline__ long long sk_begin(int q) const {
+        return static_cast<long long>(q) * sk_iters / sk_pairs;
+    }
+};
+
+// A pair's units in MMA order.  A stream-K range is at most one tile long
+// (r < P tiles over P pairs, or at most 2 * (kb / 4) blocks each), so it is
+// one unit or two: the end of tile s (a piece) and the start of
+// tile s + 1 (owned).  The owned part goes first, so that every pair starts
+// its range at K block 0 and ends it at the last K block: the pairs sweep
+// the tiles' K blocks together, which keeps A and B reads shared in L2.
+struct PairUnits {
+    int t;       // next whole tile
+    int n, i;    // stream-K units of this pair and the next one to hand out
+    PairWork u0, u1;
+    __device__ __forceinline__ void init(const PairSchedule &s, int pair) {
+        t = pair;
+        n = i = 0;
+        if (s.sk_index >= s.sk_pairs) return;
+        const long long a = s.sk_begin(s.sk_index), b = s.sk_begin(s.sk_index + 1);
+        if (b <= a) return;
+        const long long sa = a / s.kb, sb = (b - 1) / s.kb;
+        auto unit = [&](long long tile_rel, long long lo, long long hi) {
+            PairWork w;
+            w.tile = s.dp_tiles + static_cast<int>(tile_rel);
+            w.k0 = static_cast<int>(lo - tile_rel * s.kb);
+            w.k1 = static_cast<int>(hi - tile_rel * s.kb);
+            w.kind = w.k0 > 0 ? kUnitPiece : (w.k1 < s.kb ? kUnitOwner : kUnitWhole);
+            return w;
+        };
+        if (sa == sb) {
+            u0 = unit(sa, a, b);
+            n = 1;
+        } else {  // sb == sa + 1: owned start of tile sb first, then the piece of tile sa
+            u0 = unit(sb, sb * s.kb, b);
+            u1 = unit(sa, a, sb * s.kb);
+            n = 2;
+        }
+    }
+    __device__ __forceinline__ bool next(const PairSchedule &s, PairWork &w) {
+        if (t < s.dp_tiles) {
+            w = PairWork{t, 0, s.kb, kUnitWhole};
+            t += s.num_pairs;
+            return true;
+        }
+        if (i >= n) return false;
+        w = i == 0 ? u0 : u1;
+        ++i;
+        return true;
+    }
+};
+
+// A stream-K piece in the workspace: per (slot q, CTA rank, epilogue warp g)
+// 8 boxes of 4 KB; box c holds accumulator columns [32c, 32c + 32) of the
+// warp's 32 rows in the staging layout (one 128-byte row per lane, 16-byte
+// chunk j of row l at position j ^ (l mod 8)).
+constexpr int kSkBoxes = 256 / 32;
+constexpr int kLandBoxes = 12;  // 48 KB of the operand ring per epilogue warp
+
+__device__ __forceinline__ uint8_t *sk_box(const KParams &p, int q, uint32_t rank, int g, int c) {
+    const size_t box = ((static_cast<size_t>(q) * 2 + rank) * kEpilogueWarps + g) * kSkBoxes + c;
+    return reinterpret_cast<uint8_t *>(p.sk_ws) + box * kStageBoxBytes;
+}
+
+__device__ __forceinline__ int *sk_flag(const KParams &p, int q, uint32_t rank, int g) {
+    return p.sk_flags + (q * 2 + static_cast<int>(rank)) * kEpilogueWarps + g;
+}
+
+// A piece of a split tile: this warp's 32 accumulator rows (all 256 columns)
+// leave as fp32 through the staging boxes and bulk stores; once they have
+// landed the warp's flag is raised (release).
+__device__ __forceinline__ void sk_store_piece(const KParams &p, int q, uint32_t rank, int g, int lane,
+                                               uint32_t t_row, uint32_t staging, int &buf) {
+#pragma unroll 1
+    for (int c = 0; c < kSkBoxes; ++c) {
+        uint32_t r[32];
+        tmem_load_32(t_row + c * 32, r);
+        tmem_load_wait();
+        if (lane == 0) bulk_wait_group_read<1>();  // the store that last used this buffer is done reading it
+        __syncwarp();
+        const uint32_t box = staging + static_cast<uint32_t>(buf * kStageBoxBytes);
+        box_put_row(box, lane, r);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+            bulk_store(sk_box(p, q, rank, g, c), box, kStageBoxBytes);
+            bulk_commit_group();
+        }
+        buf ^= 1;
+    }
+    if (lane == 0) {
+        bulk_wait_group_all();  // the piece is in global memory
+        fence_proxy_async_global();
+        red_release_gpu_add(sk_flag(p, q, rank, g), 1);
+    }
+    __syncwarp();
+}
+
+// The owner of a split tile: wait (bounded) for the other pieces' flags,
+// bulk-load their boxes into `land` (48 KB of the idle operand ring: the
+// owner's unit is its pair's last) in rounds, add them in stream-K order to
+// this warp's accumulator rows in TMEM, clear the flags.  False when a piece
+// or a load did not arrive in time.
+__device__ __forceinline__ bool sk_fold_pieces(const KParams &p, const PairSchedule &s, const PairWork &w,
+                                               uint32_t rank, int g, int lane, uint32_t t_row, uint32_t land,
+                                               uint32_t fold_bar, const volatile int *abort_flag) {
+    const long long tile_end = static_cast<long long>(w.tile - s.dp_tiles + 1) * s.kb;
+    const int q0 = s.sk_index + 1;
+    int q_end = q0;
+    while (q_end < s.sk_pairs && s.sk_begin(q_end) < tile_end) ++q_end;
+    const int nq = q_end - q0;
+    if (nq <= 0) return true;
+    const uint64_t t0 = global_timer_ns();
+    bool ok = true;
+    for (int q = q0; ok && q < q_end; ++q) {
+        const int *f = sk_flag(p, q, rank, g);
+        while (ld_acquire_gpu(f) < 1) {
+            if (*abort_flag || global_timer_ns() - t0 > p.timeout_ns) {
+                ok = false;
+                break;
+            }
+        }
+    }
+    if (!__all_sync(0xffffffffu, ok)) return false;
+    const int per_round = kLandBoxes / nq < kSkBoxes ? kLandBoxes / nq : kSkBoxes;
+    uint32_t phase = 0;
+#pragma unroll 1
+    for (int c0 = 0; c0 < kSkBoxes; c0 += per_round) {
+        const int cn = kSkBoxes - c0 < per_round ? kSkBoxes - c0 : per_round;
+        if (lane == 0) {
+            fence_proxy_async_global();  // the acquired flags come before these async-proxy reads
+            mbar_arrive_expect_tx(fold_bar, static_cast<uint32_t>(cn * nq * kStageBoxBytes));
+            for (int i = 0; i < cn; ++i)
+                for (int j = 0; j < nq; ++j)
+                    bulk_load(land + static_cast<uint32_t>((i * nq + j) * kStageBoxBytes),
+                              sk_box(p, q0 + j, rank, g, c0 + i), kStageBoxBytes, fold_bar);
+        }
+        const bool landed = mbar_wait(fold_bar, phase, abort_flag, p.timeout_ns);
+        if (!__all_sync(0xffffffffu, landed)) return false;
+        phase ^= 1u;
+#pragma unroll 1
+        for (int i = 0; i < cn; ++i) {
+            uint32_t r[32];
+            tmem_load_32(t_row + static_cast<uint32_t>((c0 + i) * 32), r);
+            tmem_load_wait();
+            for (int j = 0; j < nq; ++j) {
+                uint32_t v[32];
+                box_get_row(land + static_cast<uint32_t>((i * nq + j) * kStageBoxBytes), lane, v);
+#pragma unroll
+                for (int k = 0; k < 32; ++k) r[k] = __float_as_uint(__fadd_rn(__uint_as_float(r[k]), __uint_as_float(v[k])));
+            }
+            tmem_store_32(t_row + static_cast<uint32_t>((c0 + i) * 32), r);
+        }
+        fence_proxy_async_smem();  // these reads come before the next round's bulk writes
+        __syncwarp();
+    }
+    tmem_store_wait();
+    __syncwarp();
+    if (lane == 0)
+        for (int q = q0; q < q_end; ++q) atomicSub(sk_flag(p, q, rank, g), 1);
+    return true;
+}
+
 struct PairCfg {
     static constexpr int kABytes = kBlockM * kRowBytes;
     static constexpr int kBBytes = kPairHalfN * kRowBytes;
@@ -512,6 +745,8 @@ struct PairCfg {
     static constexpr int kTmemCols = 512;  // two 256-column accumulators
     static constexpr int kSmemBytes = kStages * kStageBytes + kBarRegion + kCStagingBytes + 1024;
     static_assert(kSmemBytes <= 232448, "over the per-block shared memory limit");
+    static_assert(kStages * kStageBytes >= kEpilogueWarps * kLandBoxes * kStageBoxBytes,
+                  "the operand ring must hold every epilogue warp's stream-K landing slice");
 };
 
 template <int FMT, bool B_MN>
@@ -530,7 +765,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + Cfg::kStages * Cfg::kStageBytes);
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * Cfg::kStages + 5);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * Cfg::kStages + 5 + kEpilogueWarps);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
@@ -545,6 +780,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * Cfg::kStages + a); };
     auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * Cfg::kStages + 2 + a); };
     const uint32_t drain_bar = bar0 + 8u * (2 * Cfg::kStages + 4);
+    auto fold_bar = [&](int g) { return bar0 + 8u * (2 * Cfg::kStages + 5 + g); };  // stream-K landing, per epilogue warp
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < Cfg::kStages; ++s) {
@@ -556,6 +792,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             mbar_init(tempty_bar(a), 2 * kEpilogueWarps);
         }
         mbar_init(drain_bar, 1);
+        for (int g = 0; g < kEpilogueWarps; ++g) mbar_init(fold_bar(g), 1);
         *abort_flag = 0;
         fence_barrier_init();
     }
@@ -576,6 +813,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const int num_m_pairs = (p.m + 2 * kBlockM - 1) / (2 * kBlockM);
     const int num_n_pairs = (p.n + kPairN - 1) / kPairN;
     const int total = num_m_pairs * num_n_pairs;
+    PairSchedule sched;
+    sched.init(p, pair, num_pairs, total);
+    PairWork w;
 
     if (warp == 0) {
         // ------------------------------------------------ TMA producer (both CTAs)
@@ -585,12 +825,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             uint32_t ph = 0;
             int round = 0;  // passes over the ring completed
             bool ok = true;
-            for (int t = pair; ok && t < total; t += num_pairs) {
+            PairUnits units;
+            units.init(sched, pair);
+            while (ok && units.next(sched, w)) {
                 int64_t tm, tn;
-                tile_raster(num_m_pairs, num_n_pairs, kGroupM, t, tm, tn);
+                tile_raster(num_m_pairs, num_n_pairs, kGroupM, w.tile, tm, tn);
                 const int m0 = static_cast<int>(tm) * 2 * kBlockM + static_cast<int>(rank) * kBlockM;
                 const int n0 = static_cast<int>(tn) * kPairN + static_cast<int>(rank) * kPairHalfN;
-                for (int kb = 0; kb < p.num_k_blocks; ++kb) {
+                for (int kb = w.k0; kb < w.k1; ++kb) {
                     if (!mbar_wait(empty_bar(s), ph ^ 1u, abort_flag, p.timeout_ns)) {
                         ok = false;
                         break;
@@ -629,7 +871,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             uint32_t ph = 0;
             int iter = 0;
             bool ok = true;
-            for (int t = pair; ok && t < total; t += num_pairs, ++iter) {
+            PairUnits units;
+            units.init(sched, pair);
+            for (; ok && units.next(sched, w); ++iter) {
                 const int acc = iter & 1;
                 const uint32_t acc_ph = static_cast<uint32_t>(iter >> 1) & 1u;
                 if (!mbar_wait(tempty_bar(acc), acc_ph ^ 1u, abort_flag, p.timeout_ns)) {
@@ -638,7 +882,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 }
                 tc_fence_after_sync();
                 const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kPairN);
-                for (int kb = 0; kb < p.num_k_blocks; ++kb) {
+                for (int kb = w.k0; kb < w.k1; ++kb) {
                     if (!mbar_wait(full_bar(s), ph, abort_flag, p.timeout_ns)) {
                         ok = false;
                         break;
@@ -655,7 +899,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         } else {
                             bdesc = smem_desc_sw128(sb + ks * 32, 16, 1024);
                         }
-                        tc_mma_pair<kTf32>(d_tmem, adesc, bdesc, kIdesc, (kb | ks) != 0 ? 1u : 0u);
+                        tc_mma_pair<kTf32>(d_tmem, adesc, bdesc, kIdesc, (kb != w.k0 || ks != 0) ? 1u : 0u);
                     }
                     tc_commit_pair(empty_bar(s));
                     if (++s == Cfg::kStages) {
@@ -681,26 +925,39 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         int sbuf = 0;
         const uint32_t even_tempty0 = map_to_rank(tempty_bar(0), 0);
         const uint32_t odd_tfull0 = map_to_rank(tfull_bar(0), 1);
-        int iter = 0;
-        for (int t = pair; t < total; t += num_pairs, ++iter) {
-            const int acc = iter & 1;
-            const uint32_t acc_ph = static_cast<uint32_t>(iter >> 1) & 1u;
+        // one unit: idx is its position in MMA order (accumulator idx & 1);
+        // ring_free: every MMA of the pair has completed (an owner's fold lands
+        // its pieces in the operand ring)
+        auto epilogue_unit = [&](const PairWork &u, int idx, bool ring_free) -> bool {
+            const int acc = idx & 1;
+            const uint32_t acc_ph = static_cast<uint32_t>(idx >> 1) & 1u;
             int64_t tm, tn;
-            tile_raster(num_m_pairs, num_n_pairs, kGroupM, t, tm, tn);
+            tile_raster(num_m_pairs, num_n_pairs, kGroupM, u.tile, tm, tn);
             const int m0 = static_cast<int>(tm) * 2 * kBlockM + static_cast<int>(rank) * kBlockM;
             const int n0 = static_cast<int>(tn) * kPairN;
             const bool ready = mbar_wait(tfull_bar(acc), acc_ph, abort_flag, p.timeout_ns);
             if (!__all_sync(0xffffffffu, ready)) {
                 *abort_flag = 1;
                 if (lane == 0) atomicExch(p.err, kDevAbortGemmEpilogue);
-                break;
+                return false;
             }
             if (even && warp == 2 && lane == 0) mbar_arrive_cluster(odd_tfull0 + 8u * acc);
             tc_fence_after_sync();
             const int row = m0 + g * 32 + lane;
             const uint32_t t_row =
                 tmem_base + (static_cast<uint32_t>(g * 32) << 16) + static_cast<uint32_t>(acc * kPairN);
-            if (p.staged) {
+            if (u.kind == kUnitOwner &&
+                (!ring_free ||
+                 !sk_fold_pieces(p, sched, u, rank, g, lane, t_row,
+                                 smem_addr(smem) + static_cast<uint32_t>(g * kLandBoxes * kStageBoxBytes), fold_bar(g),
+                                 abort_flag))) {
+                *abort_flag = 1;
+                if (lane == 0) atomicExch(p.err, kDevAbortGemmStreamK);
+                return false;
+            }
+            if (u.kind == kUnitPiece) {
+                sk_store_piece(p, sched.sk_index, rank, g, lane, t_row, staging, sbuf);
+            } else if (p.staged) {
                 store_tile_staged<kPairN>(p, cmaps, t_row, m0 + g * 32, n0, staging, sbuf, lane);
             } else {
 #pragma unroll 1
@@ -720,6 +977,25 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 if (even) mbar_arrive(tempty_bar(acc));
                 else mbar_arrive_cluster(even_tempty0 + 8u * acc);
             }
+            return true;
+        };
+        PairUnits units;
+        units.init(sched, pair);
+        PairWork cur, nxt;
+        int idx = 0;
+        bool have_cur = units.next(sched, cur);
+        while (have_cur) {
+            const bool have_nxt = units.next(sched, nxt);
+            if (cur.kind == kUnitOwner && have_nxt) {
+                // the piece after an owned part is the pair's last MMA unit and
+                // another pair's owner waits for it: store it first
+                if (!epilogue_unit(nxt, idx + 1, false) || !epilogue_unit(cur, idx, true)) break;
+                break;
+            }
+            if (!epilogue_unit(cur, idx, !have_nxt)) break;
+            ++idx;
+            cur = nxt;
+            have_cur = have_nxt;
         }
         if (p.staged && lane == 0) bulk_wait_group_all();  // every TMA store of C has landed
     }
@@ -1241,6 +1517,8 @@ int launch_gemm_3xtf32(const GemmArgs &g, int sm_count, int *dev_err, uint64_t t
     kp.num_k_blocks = static_cast<int>(cdiv(g.k, 32));
     kp.total_tiles = kp.num_m_tiles * kp.num_n_tiles;
     kp.c = g.c;
+    kp.sk_ws = nullptr;
+    kp.sk_flags = nullptr;
     kp.staged = 0;  // direct stores
     kp.n_peers = g.peers.n;
     for (int i = 0; i < kMaxPeers; ++i) kp.c_peers[i] = i < g.peers.n ? g.peers.base[i] : nullptr;
@@ -1253,6 +1531,23 @@ int launch_gemm_3xtf32(const GemmArgs &g, int sm_count, int *dev_err, uint64_t t
     if (!g.b_k_major) return launch_x3_instance<true, 64>(ma, mb, kp, plan.ctas, stream);
     if (plan.block_n == 128) return launch_x3_instance<false, 128>(ma, mb, kp, plan.ctas, stream);
     return launch_x3_instance<false, 64>(ma, mb, kp, plan.ctas, stream);
+}
+
+// SPTILES_B200_STREAM_K=0 turns the stream-K tail of the CTA-pair kernel off
+// (whole tiles only); on by default.
+bool stream_k_enabled() {
+    const char *v = std::getenv("SPTILES_B200_STREAM_K");
+    return !(v != nullptr && v[0] == '0');
+}
+
+size_t stream_k_flag_offset(int sm_count) {
+    const int pairs = (sm_count > 0 ? sm_count : 148) / 2;
+    return static_cast<size_t>(pairs) * 2 * kPairN * kBlockM * sizeof(float);
+}
+
+size_t stream_k_workspace_bytes(int sm_count) {
+    const int pairs = (sm_count > 0 ? sm_count : 148) / 2;
+    return stream_k_flag_offset(sm_count) + static_cast<size_t>(pairs) * 2 * kEpilogueWarps * sizeof(int);
 }
 
 int plan_gemm(int in_dtype, int64_t m, int64_t n, int64_t k, int sm_count, GemmPlan *plan) {
@@ -1285,12 +1580,25 @@ int plan_gemm(int in_dtype, int64_t m, int64_t n, int64_t k, int sm_count, GemmP
             best.tiles = static_cast<int>(tiles);
         }
     }
-    // CTA pairs: 256 x 256 per pair, half the staged B bytes per SM
+    // CTA pairs: 256 x 256 per pair, half the staged B bytes per SM; a
+    // partial last wave goes out as a stream-K tail (whole-tile fill otherwise)
     {
         const int pairs = sm_count / 2;
         const int64_t tiles = cdiv(m, 2 * kBlockM) * cdiv(n, kPairN);
         const int64_t waves = cdiv(tiles, pairs);
-        const double fill = static_cast<double>(tiles) / static_cast<double>(waves * pairs);
+        double fill = static_cast<double>(tiles) / static_cast<double>(waves * pairs);
+        const int kb = static_cast<int>(cdiv(k, in_dtype == ST_F32 ? 32 : 64));
+        int dp_tiles = 0, sk_pairs = 0;
+        long long sk_iters = 0;
+        if (tiles < (int64_t(1) << 30))
+            stream_k_split(static_cast<int>(tiles), pairs, kb, stream_k_enabled(), dp_tiles, sk_pairs, sk_iters);
+        if (sk_pairs > 0) {
+            // per pair: whole tiles, its tail range, ~6 K blocks of partial store / fold
+            const double work = static_cast<double>(dp_tiles / pairs) * kb +
+                                static_cast<double>((sk_iters + sk_pairs - 1) / sk_pairs) + 6.0;
+            const double ideal = static_cast<double>(tiles) * kb / pairs;
+            fill = ideal / work < 1.0 ? ideal / work : 1.0;
+        }
         const double ncov = static_cast<double>(n) / static_cast<double>(cdiv(n, kPairN) * kPairN);
         const double mcov = static_cast<double>(m) / static_cast<double>(cdiv(m, 2 * kBlockM) * 2 * kBlockM);
         const double score = fill * ncov * mcov * 1.10;
@@ -1305,7 +1613,15 @@ int plan_gemm(int in_dtype, int64_t m, int64_t n, int64_t k, int sm_count, GemmP
     best.block_k = in_dtype == ST_F32 ? 32 : 64;
     if (best.pair) {
         best.stages = PairCfg::kStages;
-        const int pairs = best.tiles < sm_count / 2 ? best.tiles : sm_count / 2;
+        // every pair with whole tiles or a stream-K range; with fewer tiles
+        // than pairs and a split, exactly the split's pairs (the kernel
+        // derives the same split from that grid)
+        int pairs = best.tiles < sm_count / 2 ? best.tiles : sm_count / 2;
+        int dp_tiles = 0, sk_pairs = 0;
+        long long sk_iters = 0;
+        stream_k_split(best.tiles, sm_count / 2, static_cast<int>(cdiv(k, best.block_k)), stream_k_enabled(),
+                       dp_tiles, sk_pairs, sk_iters);
+        if (sk_pairs > 0) pairs = dp_tiles > 0 ? sm_count / 2 : sk_pairs;
         best.ctas = 2 * pairs;
     } else {
         best.stages = best.block_n == 256 ? TileCfg<256>::kStages
@@ -1328,13 +1644,10 @@ bool c_store_staged(const GemmArgs &g) {
     for (int d = 0; d < g.peers.n; ++d)
         if (reinterpret_cast<uintptr_t>(g.peers.base[d]) % 16 != 0) return false;
     if (g.peers.n > 0) return true;
-    static const int mode = [] {
-        const char *v = std::getenv("SPTILES_B200_C_STORE");
-        if (v != nullptr && std::strcmp(v, "direct") == 0) return 0;
-        if (v != nullptr && std::strcmp(v, "tma") == 0) return 1;
-        return ST_C_STORE_DEFAULT;
-    }();
-    return mode != 0;
+    const char *v = std::getenv("SPTILES_B200_C_STORE");
+    if (v != nullptr && std::strcmp(v, "direct") == 0) return false;
+    if (v != nullptr && std::strcmp(v, "tma") == 0) return true;
+    return ST_C_STORE_DEFAULT != 0;
 }
 
 int launch_gemm(const GemmArgs &g, int sm_count, int *dev_err, uint64_t timeout_ns, cudaStream_t stream) {
@@ -1380,6 +1693,8 @@ int launch_gemm(const GemmArgs &g, int sm_count, int *dev_err, uint64_t timeout_
     kp.bias_dtype = g.bias_dtype;
     kp.err = dev_err;
     kp.timeout_ns = timeout_ns;
+    kp.sk_ws = plan.pair && stream_k_enabled() ? g.sk_ws : nullptr;
+    kp.sk_flags = kp.sk_ws ? g.sk_flags : nullptr;
     CStoreMaps cm;
     std::memset(&cm, 0, sizeof(cm));
     kp.staged = 0;
@@ -1423,6 +1738,19 @@ extern "C" int st_tile_raster(int64_t m, int64_t n, int64_t tm, int64_t tn, int6
     const int64_t num_m = st::cdiv(m, tm), num_n = st::cdiv(n, tn);
     if (bid >= num_m * num_n) return st::fail(ST_ERR_INVALID_ARGUMENT, "st_tile_raster: bid out of range");
     st::tile_raster(num_m, num_n, group_m, bid, *bid_m, *bid_n);
+    return ST_OK;
+}
+
+extern "C" int st_stream_k_split(int32_t tiles, int32_t pairs, int32_t k_blocks, int32_t *dp_tiles,
+                                 int32_t *sk_pairs, int64_t *sk_iters) {
+    if (tiles < 0 || pairs <= 0 || k_blocks <= 0 || !dp_tiles || !sk_pairs || !sk_iters)
+        return st::fail(ST_ERR_INVALID_ARGUMENT, "st_stream_k_split: tiles >= 0, pairs and k_blocks > 0");
+    int dp = 0, skp = 0;
+    long long ski = 0;
+    st::stream_k_split(tiles, pairs, k_blocks, st::stream_k_enabled(), dp, skp, ski);
+    *dp_tiles = dp;
+    *sk_pairs = skp;
+    *sk_iters = ski;
     return ST_OK;
 }
 

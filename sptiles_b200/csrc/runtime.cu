@@ -64,6 +64,7 @@ struct DeviceState {
     int *dev_err = nullptr;
     Workspace scratch;  // packed / repacked matmul operands
     Workspace stage;    // device copies of host-memory arguments
+    Workspace sk;       // stream-K partials and flags of the CTA-pair GEMM (fixed size, flags zeroed)
     // host-memory calls: copies in and out run on their own streams so that
     // both PCIe directions overlap the kernels
     cudaStream_t copy_in = nullptr;
@@ -154,6 +155,33 @@ void ws_free(Workspace &ws) {
     ws = Workspace{};
 }
 
+// The stream-K workspace: allocated with its flags zeroed by the first
+// uncaptured matmul on the device (a capture before that runs whole tiles
+// only), then ordered across streams like the other workspaces.
+int sk_acquire(DeviceState *d, cudaStream_t stream, GemmArgs &g) {
+    if (!d->sk.ptr) {
+        if (capturing(stream)) return ST_OK;
+        const size_t bytes = stream_k_workspace_bytes(d->sm_count);
+        ST_CUDA_TRY(cudaMalloc(&d->sk.ptr, bytes));
+        d->sk.bytes = bytes;
+        ST_CUDA_TRY(cudaMemsetAsync(d->sk.ptr, 0, bytes, stream));
+    }
+    void *base = nullptr;
+    ST_TRY(ws_acquire(d->sk, d->sk.bytes, stream, &base));
+    g.sk_ws = static_cast<float *>(base);
+    g.sk_flags = reinterpret_cast<int *>(static_cast<uint8_t *>(base) + stream_k_flag_offset(d->sm_count));
+    return ST_OK;
+}
+
+// After an abort a split tile's flags may still be raised: clear them.
+void sk_reset(DeviceState *d) {
+    if (!d->sk.ptr) return;
+    DeviceGuard guard(d->ordinal);
+    const size_t off = stream_k_flag_offset(d->sm_count);
+    cudaMemset(static_cast<uint8_t *>(d->sk.ptr) + off, 0, d->sk.bytes - off);
+    cudaDeviceSynchronize();
+}
+
 // Bounded wait for `stream`, then collect a kernel abort from the error word.
 int bounded_sync(DeviceState *d, cudaStream_t stream, uint32_t timeout_ms) {
     if (timeout_ms == 0) timeout_ms = kDefaultTimeoutMs;
@@ -180,6 +208,7 @@ int bounded_sync(DeviceState *d, cudaStream_t stream, uint32_t timeout_ms) {
     ST_CUDA_TRY(cudaMemcpy(&code, d->dev_err, sizeof(int), cudaMemcpyDeviceToHost));
     if (code != 0) {
         ST_CUDA_TRY(cudaMemset(d->dev_err, 0, sizeof(int)));
+        sk_reset(d);
         return fail(ST_ERR_DEVICE_ABORT, "a kernel gave up a bounded wait (code " + std::to_string(code) + ")");
     }
     return ST_OK;
@@ -367,7 +396,9 @@ int matmul_device(const ExecCtx &x, const st_tensor &a, const st_tensor &b, cons
         g.ldb = 3 * kp;
         g.b_k_major = true;
         g.k = 3 * kp;
+        ST_TRY(sk_acquire(x.dev, x.stream, g));
         ST_TRY(launch_gemm(g, x.dev->sm_count, x.dev->dev_err, kDeviceWaitLimitNs, x.stream));
+        if (g.sk_ws) ST_TRY(ws_release(x.dev->sk, x.stream));
         return ws_release(ws, x.stream);
     }
     // 16-bit operands: use them in place when TMA can address them
@@ -410,7 +441,9 @@ int matmul_device(const ExecCtx &x, const st_tensor &a, const st_tensor &b, cons
         g.ldb = ldb_p;
         g.b_k_major = false;
     }
+    ST_TRY(sk_acquire(x.dev, x.stream, g));
     ST_TRY(launch_gemm(g, x.dev->sm_count, x.dev->dev_err, kDeviceWaitLimitNs, x.stream));
+    if (g.sk_ws) ST_TRY(ws_release(x.dev->sk, x.stream));
     if (need) return ws_release(ws, x.stream);
     return ST_OK;
 }
@@ -884,6 +917,7 @@ int st_shutdown(st_ctx *ctx) {
         if (d.copy_out) cudaStreamSynchronize(d.copy_out);
         ws_free(d.scratch);
         ws_free(d.stage);
+        ws_free(d.sk);
         for (cudaEvent_t e : d.events) cudaEventDestroy(e);
         if (d.copy_in) cudaStreamDestroy(d.copy_in);
         if (d.copy_out) cudaStreamDestroy(d.copy_out);

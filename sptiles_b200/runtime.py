@@ -175,6 +175,14 @@ def matmul_plan(in_dtype: int, m: int, n: int, k: int, sm_count: int = 148) -> d
     return dict(zip(("block_m", "block_n", "block_k", "stages", "ctas"), (o.value for o in out)))
 
 
+def stream_k_split(tiles: int, pairs: int, k_blocks: int) -> tuple[int, int, int]:
+    """(dp_tiles, sk_pairs, sk_iters) of the CTA-pair kernel's work split."""
+    dp, skp, ski = ctypes.c_int32(), ctypes.c_int32(), ctypes.c_int64()
+    N.check(N.lib().st_stream_k_split(tiles, pairs, k_blocks, ctypes.byref(dp), ctypes.byref(skp), ctypes.byref(ski)),
+            "st_stream_k_split")
+    return dp.value, skp.value, ski.value
+
+
 def shard_range(total: int, count: int, rank: int, align: int = 1) -> tuple[int, int]:
     b, e = ctypes.c_int64(), ctypes.c_int64()
     N.check(N.lib().st_shard_range(total, count, rank, align, ctypes.byref(b), ctypes.byref(e)), "st_shard_range")

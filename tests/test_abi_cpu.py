@@ -79,7 +79,12 @@ def test_matmul_plan_is_sane(dt, m, n, k):
     assert p["block_k"] * (4 if dt == N.ST_F32 else 2) == 128
     tiles = -(-m // p["block_m"]) * -(-n // p["block_n"])
     if p["block_m"] == 256:  # CTA pairs: two CTAs per tile, at most 74 pairs
-        assert p["ctas"] == 2 * min(tiles, 74)
+        kb = -(-k // 64) if dt != N.ST_F32 else 3 * -(-k // 32)  # fp32: 3 x K rounded to 32, 32-deep blocks
+        dp, skp, _ = st.stream_k_split(tiles, 74, kb)
+        if skp == 0:
+            assert p["ctas"] == 2 * min(tiles, 74)
+        else:  # a stream-K tail: all pairs, or exactly the split's pairs when no tile goes out whole
+            assert p["ctas"] == 2 * (74 if dp > 0 else skp)
     else:
         assert p["ctas"] == min(tiles, 148)
     assert 2 <= p["stages"] <= 8

@@ -301,7 +301,9 @@ def test_host_tensors_chunked_pipeline(pinned, dtype):
     C = st.matmul(A, B, bias, out_dtype=torch.float32)
     assert C.device.type == "cpu"
     Cd = st.matmul(A.to(DEV), B.to(DEV), bias.to(DEV), out_dtype=torch.float32)
-    assert rel_err(C.numpy(), Cd.cpu().numpy()) <= 1e-6
+    # the chunks and the one-call product split the partial last wave's K
+    # blocks differently (stream-K), so only the fp32 summation order differs
+    assert rel_err(C.numpy(), Cd.cpu().numpy()) <= 1e-5
     for r0, r1 in ((0, 8), (1784, 1800), (m - 8, m)):  # both chunks and the seam
         want = oracle_mm(A, B, bias, rows=(r0, r1))
         assert rel_err(C[r0:r1].numpy(), want) <= TOL[dtype]
@@ -361,3 +363,63 @@ def test_fp32_paths_random_accuracy(monkeypatch, path):
         C = st.matmul(A, Bv, bias)
         err = rel_err(C.cpu().numpy(), want)
         assert err <= 5e-5, f"{path}: 3xTF32 error {err}"
+
+
+# ------------------------------------------------------------ stream-K tail of the CTA-pair kernel
+# Shapes with fewer 256 x 256 tiles than the 74 pairs, so the tiles' K blocks
+# are split over more pairs and folded by each tile's owner (from ~1.2 to 4
+# pieces per tile; ragged M and N; 8 to 64 K blocks per tile).
+SK_SHAPES = [(1024, 4096, 1024), (256, 2048, 4096), (1000, 3000, 2000), (512, 8192, 512), (300, 520, 2000)]
+
+
+@pytest.mark.parametrize("sk", ["1", "0"], ids=["stream_k", "whole_tiles"])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16], ids=["f32", "f16", "bf16"])
+@pytest.mark.parametrize("mnk", SK_SHAPES, ids=lambda s: "x".join(map(str, s)))
+def test_stream_k_tail_known_answers(monkeypatch, sk, dtype, mnk):
+    monkeypatch.setenv("SPTILES_B200_GEMM_KERNEL", "pair")
+    monkeypatch.setenv("SPTILES_B200_STREAM_K", sk)
+    m, n, k = mnk
+    A, B = kat(m, n, k, dtype)
+    C = st.matmul(A, B, out_dtype=torch.float32)
+    assert C.cpu().numpy().tobytes() == oracle.matmul_kat_expected(m, n, k).tobytes()
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16], ids=["f16", "bf16"])
+@pytest.mark.parametrize("mnk", SK_SHAPES[:3], ids=lambda s: "x".join(map(str, s)))
+def test_stream_k_tail_random_bias_16bit_out(monkeypatch, dtype, mnk):
+    monkeypatch.setenv("SPTILES_B200_GEMM_KERNEL", "pair")
+    m, n, k = mnk
+    A, B = normal((m, k), 0.5, 80, dtype), normal((k, n), 0.5, 81, dtype)
+    bias = normal((n,), 1.0, 82, dtype)
+    rows = (max(0, m - 300), m)  # the last rows: the stream-K tiles of the raster
+    C = st.matmul(A, B, bias, out_dtype=dtype)
+    want = oracle_mm(A, B, bias, rows=rows, out=oracle.BF16 if dtype == torch.bfloat16 else oracle.F16)
+    got = to_np(C[rows[0]:rows[1]])
+    if dtype == torch.bfloat16:
+        got, want = oracle.bf16_bits_to_f32(got), oracle.bf16_bits_to_f32(want)
+    assert rel_err(np.asarray(got, np.float32).reshape(-1), np.asarray(want, np.float32).reshape(-1)) <= TOL[dtype]
+    monkeypatch.setenv("SPTILES_B200_STREAM_K", "0")
+    C0 = st.matmul(A, B, bias, out_dtype=torch.float32)
+    C1 = st.matmul(A, B, bias, out_dtype=torch.float32)  # default again below
+    monkeypatch.setenv("SPTILES_B200_STREAM_K", "1")
+    C1 = st.matmul(A, B, bias, out_dtype=torch.float32)
+    # only the summation order of the split tiles differs
+    assert rel_err(C1.cpu().numpy(), C0.cpu().numpy()) <= 1e-5
+
+
+def test_stream_k_tail_replays_from_a_cuda_graph(monkeypatch):
+    monkeypatch.setenv("SPTILES_B200_GEMM_KERNEL", "pair")
+    m, n, k = 1024, 8192, 1024
+    A, B = kat(m, n, k, torch.float16)
+    out = torch.zeros((m, n), device=DEV)
+    st.matmul(A, B, out=out)  # warm-up: allocates the stream-K workspace
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        st.matmul(A, B, out=out)
+    want = oracle.matmul_kat_expected(m, n, k).tobytes()
+    for _ in range(3):  # the flags clear themselves between replays
+        out.fill_(-1.0)
+        g.replay()
+        torch.cuda.synchronize()
+        assert out.cpu().numpy().tobytes() == want
