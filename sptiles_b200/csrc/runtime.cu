@@ -535,39 +535,49 @@ bool host_rows_dense(const st_tensor &t) {  // unit column stride (rows may be p
     return t.shape[1] <= 1 || t.strides[1] == 1;
 }
 
-// rows [r0, r1) of a rank-2 host tensor <-> a dense device block
-int copy_rows_in(cudaStream_t s, void *dst, const st_tensor &h, int64_t r0, int64_t r1) {
+// Block [r0, r1) x [c0, c1) of a rank-2 host tensor <-> the same block of a
+// device matrix with row pitch `ld` elements.
+int copy_block_in(cudaStream_t s, void *dev, int64_t ld, const st_tensor &h, int64_t r0, int64_t r1, int64_t c0,
+                  int64_t c1) {
     const size_t es = dtype_size(h.dtype);
-    const int64_t cols = h.shape[1];
-    if (r1 <= r0 || cols == 0) return ST_OK;
-    const int64_t hs0 = h.shape[0] > 1 ? h.strides[0] : cols;
-    const uint8_t *src = static_cast<const uint8_t *>(h.data) + static_cast<size_t>(r0 * hs0) * es;
-    ST_CUDA_TRY(cudaMemcpy2DAsync(dst, cols * es, src, hs0 * es, cols * es, r1 - r0, cudaMemcpyHostToDevice, s));
+    if (r1 <= r0 || c1 <= c0) return ST_OK;
+    const int64_t hs0 = h.shape[0] > 1 ? h.strides[0] : h.shape[1];
+    const uint8_t *src = static_cast<const uint8_t *>(h.data) + static_cast<size_t>(r0 * hs0 + c0) * es;
+    uint8_t *dst = static_cast<uint8_t *>(dev) + static_cast<size_t>(r0 * ld + c0) * es;
+    ST_CUDA_TRY(cudaMemcpy2DAsync(dst, ld * es, src, hs0 * es, (c1 - c0) * es, r1 - r0, cudaMemcpyHostToDevice, s));
     return ST_OK;
 }
 
-int copy_rows_out(cudaStream_t s, const st_tensor &h, const void *src, int64_t r0, int64_t r1) {
+int copy_block_out(cudaStream_t s, const st_tensor &h, const void *dev, int64_t ld, int64_t r0, int64_t r1,
+                   int64_t c0, int64_t c1) {
     const size_t es = dtype_size(h.dtype);
-    const int64_t cols = h.shape[1];
-    if (r1 <= r0 || cols == 0) return ST_OK;
-    const int64_t hs0 = h.shape[0] > 1 ? h.strides[0] : cols;
-    uint8_t *dst = static_cast<uint8_t *>(h.data) + static_cast<size_t>(r0 * hs0) * es;
-    ST_CUDA_TRY(cudaMemcpy2DAsync(dst, hs0 * es, src, cols * es, cols * es, r1 - r0, cudaMemcpyDeviceToHost, s));
+    if (r1 <= r0 || c1 <= c0) return ST_OK;
+    const int64_t hs0 = h.shape[0] > 1 ? h.strides[0] : h.shape[1];
+    uint8_t *dst = static_cast<uint8_t *>(h.data) + static_cast<size_t>(r0 * hs0 + c0) * es;
+    const uint8_t *src = static_cast<const uint8_t *>(dev) + static_cast<size_t>(r0 * ld + c0) * es;
+    ST_CUDA_TRY(cudaMemcpy2DAsync(dst, hs0 * es, src, ld * es, (c1 - c0) * es, r1 - r0, cudaMemcpyDeviceToHost, s));
     return ST_OK;
 }
 
-// C = A @ B (+ bias) on host tensors with 16-bit A and B:
-//   copy_in : B (and bias), then A in row chunks
-//   compute : chunk i's GEMM once its rows of A are in
-//   copy_out: chunk i's rows of C once its GEMM is done
+// C = A @ B (+ bias) on host tensors with 16-bit A and B.  C[i, j] needs row
+// i of A and column j of B, so the received rows of A and columns of B grow
+// together: step s brings row block s of A and column block s of B (~16 MB
+// each) on copy_in, then computes on the caller's stream
+//   C[new rows, all columns so far]  and  C[earlier rows, new columns]
+// and sends those blocks of C back on copy_out.  With A and B arriving in
+// step, C comes out from the first ~2 blocks on and both PCIe directions
+// stay busy (with B first, nothing leaves until all of B is in).  Device
+// copies use row pitches rounded up to 8 elements, so every block view is a
+// 16-byte-aligned TMA operand.
 int matmul_host_pipelined(const ExecCtx &x, const st_tensor &a, const st_tensor &b, const st_tensor *bias,
                           const st_tensor &c) {
     DeviceState *d = x.dev;
     ST_TRY(ensure_copy_streams(d));
     const int64_t M = a.shape[0], K = a.shape[1], N = b.shape[1];
     const size_t ein = dtype_size(a.dtype), eout = dtype_size(c.dtype);
-    const size_t a_bytes = static_cast<size_t>(M * K) * ein, b_bytes = static_cast<size_t>(K * N) * ein;
-    const size_t c_bytes = static_cast<size_t>(M * N) * eout;
+    const int64_t lda = cdiv(K, 8) * 8, ldb = cdiv(N, 8) * 8, ldc = cdiv(N, 8) * 8;
+    const size_t a_bytes = static_cast<size_t>(M * lda) * ein, b_bytes = static_cast<size_t>(K * ldb) * ein;
+    const size_t c_bytes = static_cast<size_t>(M * ldc) * eout;
     const size_t bias_bytes = bias ? static_cast<size_t>(N) * dtype_size(bias->dtype) : 0;
     auto up = [](size_t v) { return (v + 255) & ~size_t(255); };
     void *base = nullptr;
@@ -580,40 +590,46 @@ int matmul_host_pipelined(const ExecCtx &x, const st_tensor &a, const st_tensor 
     // the copies start after earlier work on the caller's stream (workspace reuse)
     ST_TRY(stream_after(d, ev, d->copy_in, x.stream));
     ST_TRY(stream_after(d, ev, d->copy_out, x.stream));
-    ST_TRY(copy_rows_in(d->copy_in, db, b, 0, K));
     if (bias) ST_CUDA_TRY(cudaMemcpyAsync(dbias, bias->data, bias_bytes, cudaMemcpyHostToDevice, d->copy_in));
-    ST_TRY(stream_after(d, ev, x.stream, d->copy_in));
-    // ~16 MB of A per chunk, in whole 256-row tiles
-    int64_t rows = static_cast<int64_t>((size_t(16) << 20) / std::max<size_t>(1, static_cast<size_t>(K) * ein));
-    rows = std::max<int64_t>(256, (rows / 256) * 256);
-    st_tensor vb = b;
-    vb.data = db;
-    vb.strides[0] = N;
-    vb.strides[1] = 1;
-    st_tensor vbias;
-    if (bias) {
-        vbias = *bias;
-        vbias.data = dbias;
-        vbias.strides[0] = 1;
-    }
-    for (int64_t r0 = 0; r0 < M; r0 += rows) {
-        const int64_t r1 = std::min(M, r0 + rows);
-        uint8_t *da_i = da + static_cast<size_t>(r0 * K) * ein;
-        uint8_t *dc_i = dc + static_cast<size_t>(r0 * N) * eout;
-        ST_TRY(copy_rows_in(d->copy_in, da_i, a, r0, r1));
+    // ~16 MB blocks, whole 256-row / 256-column tiles
+    const int64_t per = static_cast<int64_t>((size_t(16) << 20) / std::max<size_t>(1, static_cast<size_t>(K) * ein));
+    const int64_t rows = std::max<int64_t>(256, (per / 256) * 256), cols = rows;
+    const int64_t steps = std::max(cdiv(M, rows), cdiv(N, cols));
+    auto view = [](const st_tensor &like, void *data, int64_t r, int64_t q, int64_t ld) {
+        st_tensor v = like;
+        v.data = data;
+        v.rank = 2;
+        v.shape[0] = r;
+        v.shape[1] = q;
+        v.strides[0] = ld;
+        v.strides[1] = 1;
+        return v;
+    };
+    auto gemm = [&](int64_t r0, int64_t r1, int64_t c0, int64_t c1) -> int {
+        if (r1 <= r0 || c1 <= c0) return ST_OK;
+        const st_tensor va = view(a, da + static_cast<size_t>(r0 * lda) * ein, r1 - r0, K, lda);
+        const st_tensor vb = view(b, db + static_cast<size_t>(c0) * ein, K, c1 - c0, ldb);
+        const st_tensor vc = view(c, dc + static_cast<size_t>(r0 * ldc + c0) * eout, r1 - r0, c1 - c0, ldc);
+        st_tensor vbias;
+        if (bias) {
+            vbias = *bias;
+            vbias.data = dbias + static_cast<size_t>(c0) * dtype_size(bias->dtype);
+            vbias.shape[0] = c1 - c0;
+            vbias.strides[0] = 1;
+        }
+        return matmul_device(x, va, vb, bias ? &vbias : nullptr, vc);
+    };
+    for (int64_t st = 0; st < steps; ++st) {
+        const int64_t r0 = std::min(M, st * rows), r1 = std::min(M, (st + 1) * rows);
+        const int64_t c0 = std::min(N, st * cols), c1 = std::min(N, (st + 1) * cols);
+        ST_TRY(copy_block_in(d->copy_in, da, lda, a, r0, r1, 0, K));
+        ST_TRY(copy_block_in(d->copy_in, db, ldb, b, 0, K, c0, c1));
         ST_TRY(stream_after(d, ev, x.stream, d->copy_in));
-        st_tensor va = a, vc = c;
-        va.data = da_i;
-        va.shape[0] = r1 - r0;
-        va.strides[0] = K;
-        va.strides[1] = 1;
-        vc.data = dc_i;
-        vc.shape[0] = r1 - r0;
-        vc.strides[0] = N;
-        vc.strides[1] = 1;
-        ST_TRY(matmul_device(x, va, vb, bias ? &vbias : nullptr, vc));
+        ST_TRY(gemm(r0, r1, 0, c1));  // new rows x every column so far
+        ST_TRY(gemm(0, r0, c0, c1));  // earlier rows x the new columns
         ST_TRY(stream_after(d, ev, d->copy_out, x.stream));
-        ST_TRY(copy_rows_out(d->copy_out, c, dc_i, r0, r1));
+        ST_TRY(copy_block_out(d->copy_out, c, dc, ldc, r0, r1, 0, c1));
+        ST_TRY(copy_block_out(d->copy_out, c, dc, ldc, 0, r0, c0, c1));
     }
     ST_TRY(stream_after(d, ev, x.stream, d->copy_out));
     ST_TRY(ws_release(d->stage, x.stream));

@@ -313,6 +313,27 @@ def test_host_tensors_chunked_pipeline(pinned, dtype):
     assert torch.equal(out[:, :n], C) and torch.all(out[:, n:] == 7.0)
 
 
+@pytest.mark.parametrize("out_dtype", [torch.float32, torch.bfloat16], ids=["f32_out", "bf16_out"])
+def test_host_tensors_row_and_column_blocks(out_dtype):
+    """K = 16380 makes ~16 MB blocks of 512 rows of A / 512 columns of B: 3 row
+    and 4 column blocks, 4 steps; K and N not multiples of 8 (padded device
+    pitches), a padded host C."""
+    m, n, k = 1300, 1700, 16380
+    dtype = torch.bfloat16
+    A, B = normal((m, k), 0.2, 95, dtype).cpu().pin_memory(), normal((k, n), 0.2, 96, dtype).cpu().pin_memory()
+    bias = normal((n,), 1.0, 97, torch.float32).cpu()
+    out = torch.full((m, n + 5), 3.0, dtype=out_dtype)
+    C = st.matmul(A, B, bias, out=out[:, :n])
+    assert torch.all(out[:, n:] == 3.0)
+    Cd = st.matmul(A.to(DEV), B.to(DEV), bias.to(DEV), out_dtype=out_dtype).cpu()
+    assert rel_err(C.float().numpy(), Cd.float().numpy()) <= (1e-5 if out_dtype == torch.float32 else 8e-3)
+    for r0, r1 in ((0, 6), (509, 515), (1021, 1027), (m - 6, m)):  # the row-block seams
+        want = oracle_mm(A, B, bias, rows=(r0, r1))
+        assert rel_err(C[r0:r1].float().numpy(), want) <= TOL[dtype]
+    for c0, c1 in ((509, 515), (1533, 1539), (n - 6, n)):  # the column-block seams
+        assert rel_err(C[:, c0:c1].float().numpy(), Cd[:, c0:c1].float().numpy()) <= 8e-3
+
+
 @pytest.mark.parametrize("dtype", [torch.float32, torch.float16], ids=["f32", "f16"])
 def test_calls_replay_from_a_cuda_graph(dtype):
     """Device-tensor calls issued inside torch.cuda.graph replay correctly."""
