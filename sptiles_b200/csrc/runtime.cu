@@ -591,7 +591,8 @@ int matmul_host_pipelined(const ExecCtx &x, const st_tensor &a, const st_tensor 
     ST_TRY(stream_after(d, ev, d->copy_in, x.stream));
     ST_TRY(stream_after(d, ev, d->copy_out, x.stream));
     if (bias) ST_CUDA_TRY(cudaMemcpyAsync(dbias, bias->data, bias_bytes, cudaMemcpyHostToDevice, d->copy_in));
-    // ~16 MB blocks, whole 256-row / 256-column tiles
+    // ~16 MB blocks in whole 256-row / 256-column tiles (measured on B200 at
+    // 8192^3: wider column blocks or taller row blocks were 2-4 % slower)
     const int64_t per = static_cast<int64_t>((size_t(16) << 20) / std::max<size_t>(1, static_cast<size_t>(K) * ein));
     const int64_t rows = std::max<int64_t>(256, (per / 256) * 256), cols = rows;
     const int64_t steps = std::max(cdiv(M, rows), cdiv(N, cols));
