@@ -133,6 +133,9 @@ int launch_pack_a_tf32(const float *a, int64_t sa0, int64_t sa1, int64_t m, int6
                        cudaStream_t stream);
 int launch_pack_b_tf32(const float *b, int64_t sb0, int64_t sb1, int64_t k, int64_t n, float *bp, int64_t kp,
                        cudaStream_t stream);
+// both in one launch (B's transposing blocks first, then A's rows)
+int launch_pack_ab_tf32(const float *a, int64_t sa0, int64_t sa1, int64_t m, const float *b, int64_t sb0,
+                        int64_t sb1, int64_t n, int64_t k, float *ap, float *bp, int64_t kp, cudaStream_t stream);
 // Copy a 16-bit [rows, cols] matrix with arbitrary element strides into a
 // dense row-major [rows, ld] buffer (ld >= cols, padding columns zeroed).
 int launch_repack_16(const uint16_t *src, int64_t s0, int64_t s1, int64_t rows, int64_t cols, uint16_t *dst,

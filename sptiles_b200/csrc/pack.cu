@@ -90,6 +90,60 @@ __global__ void __launch_bounds__(kThreads) pack_b_kernel(const float *__restric
     }
 }
 
+// Both operands in one launch: blocks [0, tiles_b) transpose B's 32 x 32
+// tiles (as pack_b_kernel), the rest split A's rows (as pack_a_kernel).
+__global__ void __launch_bounds__(kThreads) pack_ab_kernel(const float *__restrict__ a, int64_t sa0, int64_t sa1,
+                                                           int64_t m, const float *__restrict__ b, int64_t sb0,
+                                                           int64_t sb1, int64_t n, int64_t k, int64_t kp,
+                                                           float *__restrict__ ap, float *__restrict__ bp,
+                                                           int tiles_k, int tiles_b) {
+    __shared__ float hi_t[32][33];
+    __shared__ float lo_t[32][33];
+    if (static_cast<int>(blockIdx.x) < tiles_b) {
+        const int64_t k0 = static_cast<int64_t>(blockIdx.x % tiles_k) * 32;
+        const int64_t n0 = static_cast<int64_t>(blockIdx.x / tiles_k) * 32;
+        const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8
+        for (int r = ty; r < 32; r += 8) {
+            const int64_t kk = k0 + r, nn = n0 + tx;
+            const float x = (kk < k && nn < n) ? b[kk * sb0 + nn * sb1] : 0.0f;
+            const float h = tf32_round(x);
+            hi_t[r][tx] = h;
+            lo_t[r][tx] = tf32_round(x - h);
+        }
+        __syncthreads();
+        for (int r = ty; r < 32; r += 8) {
+            const int64_t nn = n0 + r, kk = k0 + tx;
+            if (nn < n && kk < kp) {
+                float *row = bp + nn * 3 * kp;
+                const float h = hi_t[tx][r];
+                row[kk] = h;
+                row[kp + kk] = lo_t[tx][r];
+                row[2 * kp + kk] = h;
+            }
+        }
+        return;
+    }
+    const int64_t groups = kp / 4;
+    const int64_t total = m * groups;
+    const int64_t step = static_cast<int64_t>(gridDim.x - tiles_b) * kThreads;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x - tiles_b) * kThreads + threadIdx.x; i < total; i += step) {
+        const int64_t r = i / groups;
+        const int64_t k0 = (i - r * groups) * 4;
+        float hi[4], lo[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float x = (k0 + j < k) ? a[r * sa0 + (k0 + j) * sa1] : 0.0f;
+            hi[j] = tf32_round(x);
+            lo[j] = tf32_round(x - hi[j]);
+        }
+        float4 *row = reinterpret_cast<float4 *>(ap + r * 3 * kp);
+        const float4 h = make_float4(hi[0], hi[1], hi[2], hi[3]);
+        row[k0 / 4] = h;
+        row[(kp + k0) / 4] = h;
+        row[(2 * kp + k0) / 4] = make_float4(lo[0], lo[1], lo[2], lo[3]);
+    }
+}
+
 __global__ void __launch_bounds__(kThreads) repack_16_kernel(const uint16_t *__restrict__ src, int64_t s0,
                                                              int64_t s1, int64_t rows, int64_t cols,
                                                              uint16_t *__restrict__ dst, int64_t ld) {
@@ -128,6 +182,22 @@ int launch_pack_b_tf32(const float *b, int64_t sb0, int64_t sb1, int64_t k, int6
     note_launch();
     const cudaError_t e = cudaPeekAtLastError();
     return e == cudaSuccess ? ST_OK : cuda_fail(cudaGetLastError(), "pack_b_kernel");
+}
+
+int launch_pack_ab_tf32(const float *a, int64_t sa0, int64_t sa1, int64_t m, const float *b, int64_t sb0,
+                        int64_t sb1, int64_t n, int64_t k, float *ap, float *bp, int64_t kp, cudaStream_t stream) {
+    if (kp <= 0 || (m <= 0 && n <= 0)) return ST_OK;
+    const int64_t tiles_k = cdiv(kp, 32);
+    const int64_t tiles_b = n > 0 ? tiles_k * cdiv(n, 32) : 0;
+    const int64_t blocks_a = m > 0 ? grid_1d(m * (kp / 4)) : 0;
+    if (tiles_b + blocks_a > (int64_t(1) << 31) - 1)
+        return fail(ST_ERR_UNSUPPORTED, "fp32 operands too large for one pack launch");
+    pack_ab_kernel<<<static_cast<unsigned>(tiles_b + blocks_a), kThreads, 0, stream>>>(
+        a, sa0, sa1, blocks_a > 0 ? m : 0, b, sb0, sb1, n, k, kp, ap, bp, static_cast<int>(tiles_k),
+        static_cast<int>(tiles_b));
+    note_launch();
+    const cudaError_t e = cudaPeekAtLastError();
+    return e == cudaSuccess ? ST_OK : cuda_fail(cudaGetLastError(), "pack_ab_kernel");
 }
 
 int launch_repack_16(const uint16_t *src, int64_t s0, int64_t s1, int64_t rows, int64_t cols, uint16_t *dst,

@@ -385,10 +385,9 @@ int matmul_device(const ExecCtx &x, const st_tensor &a, const st_tensor &b, cons
         ST_TRY(ws_acquire(ws, need, x.stream, &base));
         float *ap = static_cast<float *>(base);
         float *bp = ap + M * 3 * kp;
-        ST_TRY(launch_pack_a_tf32(static_cast<const float *>(a.data), a.strides[0], a.strides[1], M, K, ap, kp,
-                                  x.stream));
-        ST_TRY(launch_pack_b_tf32(static_cast<const float *>(b.data), b.strides[0], b.strides[1], K, N, bp, kp,
-                                  x.stream));
+        ST_TRY(launch_pack_ab_tf32(static_cast<const float *>(a.data), a.strides[0], a.strides[1], M,
+                                   static_cast<const float *>(b.data), b.strides[0], b.strides[1], N, K, ap, bp, kp,
+                                   x.stream));
         g.ab_dtype = ST_F32;
         g.a = ap;
         g.lda = 3 * kp;

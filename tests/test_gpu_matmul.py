@@ -444,3 +444,30 @@ def test_stream_k_tail_replays_from_a_cuda_graph(monkeypatch):
         g.replay()
         torch.cuda.synchronize()
         assert out.cpu().numpy().tobytes() == want
+
+
+# ------------------------------------------------------------ bounded host waits
+def test_bounded_host_wait_times_out_then_the_work_completes():
+    """st_sync with a 1 ms limit on ~15 ms of queued GEMMs returns
+    ST_ERR_TIMEOUT (TimeoutError) without disturbing the GPU; a later wait
+    completes and the results are exact."""
+    ctx = st.context(0)
+    sp = ctypes.c_void_p()
+    N.check(N.lib().st_stream(ctx, 0, ctypes.byref(sp)), "st_stream")
+    s = torch.cuda.ExternalStream(sp.value, device=DEV)
+    m, n, k = 8192, 8192, 8192
+    A, B = kat(m, n, k, torch.float16)
+    C = torch.zeros((m, n), device=DEV)
+    torch.cuda.synchronize()
+    with torch.cuda.stream(s):
+        for _ in range(20):
+            st.matmul(A, B, out=C)
+    with pytest.raises(TimeoutError):
+        st.sync(0, timeout_ms=1)
+    st.sync(0, timeout_ms=60000)
+    assert C.cpu().numpy().tobytes() == oracle.matmul_kat_expected(m, n, k).tobytes()
+    with torch.cuda.stream(s):
+        C.zero_()
+        st.matmul(A, B, out=C)
+    st.sync(0, timeout_ms=60000)
+    assert C.cpu().numpy().tobytes() == oracle.matmul_kat_expected(m, n, k).tobytes()
