@@ -262,7 +262,12 @@ __device__ __forceinline__ void store_tile_staged(const KParams &p, const CStore
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
+#if ST_C_POLICY == 1
+            const uint64_t pol = l2_policy_evict_first();
+            for (int d = 0; d <= p.n_peers; ++d) tma_store_2d_hint(&cm.map[d], box, col0, row0, pol);
+#else
             for (int d = 0; d <= p.n_peers; ++d) tma_store_2d(&cm.map[d], box, col0, row0);
+#endif
             bulk_commit_group();
         }
         buf ^= 1;
@@ -511,16 +516,31 @@ constexpr int kPairHalfN = 128;  // columns of B each CTA stages
 #define ST_PAIR_STAGES 6
 #endif
 #ifndef ST_L2_POLICY
-#define ST_L2_POLICY 1  // operand loads: 0 evict_normal, 1 evict_last
+// operand loads: 0 evict_normal, 1 evict_last, 2 A evict_last and B evict_first
+#define ST_L2_POLICY 1
 #endif
 
-__device__ __forceinline__ uint64_t operand_l2_policy() {
-#if ST_L2_POLICY == 1
-    return l2_policy_evict_last();
-#else
+__device__ __forceinline__ uint64_t l2_policy_evict_normal() {
     uint64_t p;
     asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(p));
     return p;
+}
+
+__device__ __forceinline__ uint64_t operand_l2_policy_a() {
+#if ST_L2_POLICY == 0
+    return l2_policy_evict_normal();
+#else
+    return l2_policy_evict_last();
+#endif
+}
+
+__device__ __forceinline__ uint64_t operand_l2_policy_b() {
+#if ST_L2_POLICY == 0
+    return l2_policy_evict_normal();
+#elif ST_L2_POLICY == 2
+    return l2_policy_evict_first();
+#else
+    return l2_policy_evict_last();
 #endif
 }
 
@@ -820,7 +840,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     if (warp == 0) {
         // ------------------------------------------------ TMA producer (both CTAs)
         if (lane == 0) {
-            const uint64_t pol = operand_l2_policy();
+            const uint64_t pol_a = operand_l2_policy_a(), pol_b = operand_l2_policy_b();
             int s = 0;
             uint32_t ph = 0;
             int round = 0;  // passes over the ring completed
@@ -844,13 +864,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     const uint32_t sa = smem_addr(smem + s * Cfg::kStageBytes);
                     const uint32_t sb = sa + Cfg::kABytes;
                     const uint32_t fb = even_full0 + 8u * s;
-                    tma_load_2d_pair(sa, &tmap_a, fb, kb * kBK, m0, pol);
+                    tma_load_2d_pair(sa, &tmap_a, fb, kb * kBK, m0, pol_a);
                     if constexpr (B_MN) {
 #pragma unroll
                         for (int j = 0; j < kPairHalfN / 64; ++j)
-                            tma_load_2d_pair(sb + j * (kBK * 128), &tmap_b, fb, n0 + 64 * j, kb * kBK, pol);
+                            tma_load_2d_pair(sb + j * (kBK * 128), &tmap_b, fb, n0 + 64 * j, kb * kBK, pol_b);
                     } else {
-                        tma_load_2d_pair(sb, &tmap_b, fb, kb * kBK, n0, pol);
+                        tma_load_2d_pair(sb, &tmap_b, fb, kb * kBK, n0, pol_b);
                     }
                     if (++s == Cfg::kStages) {
                         s = 0;

@@ -91,6 +91,15 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, uint32_t sr
                  : "memory");
 }
 
+// The same store with an L2 cache policy (createpolicy) on the written lines.
+__device__ __forceinline__ void tma_store_2d_hint(const CUtensorMap *map, uint32_t src, int32_t c0, int32_t c1,
+                                                  uint64_t policy) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group.L2::cache_hint [%0, {%2, %3}], [%1], %4;" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(src), "r"(c0), "r"(c1), "l"(policy)
+                 : "memory");
+}
+
 __device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 
 // Untiled bulk copies (both addresses 16-byte aligned, size a multiple of 16).
