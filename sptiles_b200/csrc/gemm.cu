@@ -88,6 +88,7 @@ struct KParams {
     int m, n, k;
     int num_m_tiles, num_n_tiles, num_k_blocks, total_tiles;
     float *sk_ws;    // stream-K partials (CTA-pair kernel); null: whole tiles only
+    int sk_mode;     // stream_k_split mode
     int *sk_flags;   // per (pair, CTA, epilogue warp): partials stored and not yet folded
     void *c;
     void *c_peers[kMaxPeers];  // the same rows of C in other GPUs' copies (may be empty)
@@ -220,12 +221,13 @@ __device__ __forceinline__ void box_get_row(uint32_t box, int lane, uint32_t (&w
 // has finished reading shared memory.  TMA clips the box at C's extents.
 template <int NCOLS>
 __device__ __forceinline__ void store_tile_staged(const KParams &p, const CStoreMaps &cm, uint32_t t_row, int row0,
-                                                  int n0, uint32_t staging, int &buf, int lane) {
+                                                  int n0, uint32_t staging, int &buf, int lane, int c_begin = 0,
+                                                  int c_end = NCOLS) {
     if (row0 >= p.m) return;
     const bool f32 = p.c_dtype == ST_F32;
     const int box_cols = f32 ? 32 : 64;
 #pragma unroll 1
-    for (int c0 = 0; c0 < NCOLS; c0 += box_cols) {
+    for (int c0 = c_begin; c0 < c_end; c0 += box_cols) {
         const int col0 = n0 + c0;
         if (col0 >= p.n) break;
         uint32_t w[32];  // this lane's 128-byte row of the box
@@ -520,11 +522,13 @@ constexpr int kPairHalfN = 128;  // columns of B each CTA stages
 #define ST_L2_POLICY 1
 #endif
 
+#if ST_L2_POLICY == 0
 __device__ __forceinline__ uint64_t l2_policy_evict_normal() {
     uint64_t p;
     asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(p));
     return p;
 }
+#endif
 
 __device__ __forceinline__ uint64_t operand_l2_policy_a() {
 #if ST_L2_POLICY == 0
@@ -552,29 +556,32 @@ __device__ __forceinline__ uint64_t operand_l2_policy_b() {
 // (T < P) that would leave P - T pairs idle; instead the T * KB K blocks are
 // split into equal contiguous ranges over S > T pairs (at least KB / 4 blocks
 // each, so a tile has at most ~5 pieces).  The split is written for a tail
-// after whole-tile waves too (dp_tiles > 0), but measured no faster there.  The pair whose range holds a split tile's first K block owns the
-// tile: it adds the other pieces' fp32 partials to its accumulator and runs
-// the epilogue.  The other pieces come first in their pairs' ranges (a range
-// starts inside the tile), so their partials are long stored when the owner,
-// which reaches the tile at the end of its range, needs them.  Stream-K
-// index q = P - 1 - pair: a contributor has a lower pair number than its
-// owner, and nothing a contributor does waits on an owner.
-enum : int { kUnitWhole = 0, kUnitOwner = 1, kUnitPiece = 2 };
+// after whole-tile waves too (dp_tiles > 0).  A split tile's units finish
+// together and reduce-scatter: each publishes the output columns the others
+// own (fp32, without waiting), then waits for the others' parts of its own
+// columns, adds them and stores those columns of C.  No unit waits before
+// every unit of its pair has published, and the grid never exceeds the
+// co-resident clusters, so the waits end.  Stream-K index q = P - 1 - pair.
+enum : int { kUnitWhole = 0, kUnitSplit = 1 };
 
 struct PairWork {
     int tile, k0, k1, kind;
 };
 
-__host__ __device__ __forceinline__ void stream_k_split(int total, int num_pairs, int kb, bool enabled, int &dp_tiles,
+// mode 0: whole tiles only; 1: split when there are fewer tiles than pairs;
+// 2: also split the partial last wave after whole-tile waves (when its idle
+// pairs cost >= 3 % of the launch)
+__host__ __device__ __forceinline__ void stream_k_split(int total, int num_pairs, int kb, int mode, int &dp_tiles,
                                                         int &sk_pairs, long long &sk_iters) {
     dp_tiles = total;
     sk_pairs = 0;
     sk_iters = 0;
-    // only with fewer tiles than pairs: with a whole tile for every pair first,
-    // the balanced tail's fold and extra stores cost what the idle pairs of a
-    // whole-tile tail do (B200, 8192 x 8192 K, 1024 and 2048 rows: -3 % / +1 %)
-    if (!enabled || num_pairs <= 0 || total >= num_pairs || total == 0 || kb < 8) return;
-    const int r = total;
+    if (mode <= 0 || num_pairs <= 0 || total == 0 || kb < 8) return;
+    if (total >= num_pairs && mode < 2) return;
+    const int r = total % num_pairs;
+    if (r == 0) return;
+    const long long full = total / num_pairs;
+    if (full > 0 && static_cast<long long>(num_pairs - r) * 100 < 3LL * num_pairs * (full + 1)) return;
     const long long iters = static_cast<long long>(r) * kb;
     const long long per = kb / 4 > 4 ? kb / 4 : 4;
     long long s = iters / per;
@@ -591,7 +598,7 @@ struct PairSchedule {
     __device__ __forceinline__ void init(const KParams &p, int pair, int num_pairs_, int total) {
         num_pairs = num_pairs_;
         kb = p.num_k_blocks;
-        stream_k_split(total, num_pairs, kb, p.sk_ws != nullptr, dp_tiles, sk_pairs, sk_iters);
+        stream_k_split(total, num_pairs, kb, p.sk_ws != nullptr ? p.sk_mode : 0, dp_tiles, sk_pairs, sk_iters);
         sk_index = num_pairs - 1 - pair;
     }
     __device__ __forceinline__ long long sk_begin(int q) const {
@@ -621,7 +628,7 @@ struct PairUnits {
             w.tile = s.dp_tiles + static_cast<int>(tile_rel);
             w.k0 = static_cast<int>(lo - tile_rel * s.kb);
             w.k1 = static_cast<int>(hi - tile_rel * s.kb);
-            w.kind = w.k0 > 0 ? kUnitPiece : (w.k1 < s.kb ? kUnitOwner : kUnitWhole);
+            w.kind = (w.k0 > 0 || w.k1 < s.kb) ? kUnitSplit : kUnitWhole;
             return w;
         };
         if (sa == sb) {
@@ -653,22 +660,60 @@ struct PairUnits {
 constexpr int kSkBoxes = 256 / 32;
 constexpr int kLandBoxes = 12;  // 48 KB of the operand ring per epilogue warp
 
-__device__ __forceinline__ uint8_t *sk_box(const KParams &p, int q, uint32_t rank, int g, int c) {
-    const size_t box = ((static_cast<size_t>(q) * 2 + rank) * kEpilogueWarps + g) * kSkBoxes + c;
+// Workspace slot of the unit of stream-K index q that covers tile `rel` (0-based
+// among the split tiles): a range covers at most two tiles, so each index
+// owns slots 2q (the tile its range starts in) and 2q + 1 (the next one).
+__device__ __forceinline__ int sk_slot(const PairSchedule &s, int q, long long rel) {
+    return 2 * q + (rel == s.sk_begin(q) / s.kb ? 0 : 1);
+}
+
+__device__ __forceinline__ uint8_t *sk_box(const KParams &p, int slot, uint32_t rank, int g, int c) {
+    const size_t box = ((static_cast<size_t>(slot) * 2 + rank) * kEpilogueWarps + g) * kSkBoxes + c;
     return reinterpret_cast<uint8_t *>(p.sk_ws) + box * kStageBoxBytes;
 }
 
-__device__ __forceinline__ int *sk_flag(const KParams &p, int q, uint32_t rank, int g) {
-    return p.sk_flags + (q * 2 + static_cast<int>(rank)) * kEpilogueWarps + g;
+__device__ __forceinline__ int *sk_flag(const KParams &p, int slot, uint32_t rank, int g) {
+    return p.sk_flags + (slot * 2 + static_cast<int>(rank)) * kEpilogueWarps + g;
 }
 
-// A piece of a split tile: this warp's 32 accumulator rows (all 256 columns)
-// leave as fp32 through the staging boxes and bulk stores; once they have
-// landed the warp's flag is raised (release).
-__device__ __forceinline__ void sk_store_piece(const KParams &p, int q, uint32_t rank, int g, int lane,
-                                               uint32_t t_row, uint32_t staging, int &buf) {
+// The units of one split tile: stream-K slots q0 .. q0 + n - 1 hold its K
+// blocks in order; this unit is number j.  The tile's output boxes (8 of 32
+// fp32 columns, or 4 of 64 16-bit columns, per row quarter) are divided
+// among the units: unit j reduces and stores boxes [nb j / n, nb (j + 1) / n).
+struct SplitTile {
+    int q0, n, j;
+    long long rel;       // the tile among the split tiles
+    int c_begin, c_end;  // this unit's own accumulator columns [c_begin, c_end)
+};
+
+__device__ __forceinline__ SplitTile split_tile(const KParams &p, const PairSchedule &s, const PairWork &w) {
+    const long long tile_start = static_cast<long long>(w.tile - s.dp_tiles) * s.kb, tile_end = tile_start + s.kb;
+    int q0 = s.sk_index;
+    while (q0 > 0 && s.sk_begin(q0) > tile_start) --q0;
+    int q1 = s.sk_index + 1;
+    while (q1 < s.sk_pairs && s.sk_begin(q1) < tile_end) ++q1;
+    SplitTile t;
+    t.q0 = q0;
+    t.n = q1 - q0;
+    t.j = s.sk_index - q0;
+    t.rel = w.tile - s.dp_tiles;
+    const int nb = p.c_dtype == ST_F32 ? 8 : 4, box_cols = 256 / nb;
+    t.c_begin = nb * t.j / t.n * box_cols;
+    t.c_end = nb * (t.j + 1) / t.n * box_cols;
+    return t;
+}
+
+// Reduce-scatter, step 1 (never waits): this warp's 32 accumulator rows of
+// every column chunk outside the unit's own range leave as fp32 through the
+// staging boxes and bulk stores to the unit's workspace slot; once they have
+// landed the warp's flag is raised by n - 1 (one per reader, release).
+__device__ __forceinline__ void sk_publish(const KParams &p, const PairSchedule &s, const SplitTile &t,
+                                           uint32_t rank, int g, int lane, uint32_t t_row, uint32_t staging,
+                                           int &buf) {
+    const int slot = sk_slot(s, t.q0 + t.j, t.rel);
 #pragma unroll 1
     for (int c = 0; c < kSkBoxes; ++c) {
+        if (c * 32 >= t.c_begin && c * 32 < t.c_end) continue;
         uint32_t r[32];
         tmem_load_32(t_row + c * 32, r);
         tmem_load_wait();
@@ -679,82 +724,103 @@ __device__ __forceinline__ void sk_store_piece(const KParams &p, int q, uint32_t
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-            bulk_store(sk_box(p, q, rank, g, c), box, kStageBoxBytes);
+            bulk_store(sk_box(p, slot, rank, g, c), box, kStageBoxBytes);
             bulk_commit_group();
         }
         buf ^= 1;
     }
     if (lane == 0) {
-        bulk_wait_group_all();  // the piece is in global memory
+        bulk_wait_group_all();  // the chunks are in global memory
         fence_proxy_async_global();
-        red_release_gpu_add(sk_flag(p, q, rank, g), 1);
+        red_release_gpu_add(sk_flag(p, slot, rank, g), t.n - 1);
     }
     __syncwarp();
 }
 
-// The owner of a split tile: wait (bounded) for the other pieces' flags,
-// bulk-load their boxes into `land` (48 KB of the idle operand ring: the
-// owner's unit is its pair's last) in rounds, add them in stream-K order to
-// this warp's accumulator rows in TMEM, clear the flags.  False when a piece
-// or a load did not arrive in time.
-__device__ __forceinline__ bool sk_fold_pieces(const KParams &p, const PairSchedule &s, const PairWork &w,
-                                               uint32_t rank, int g, int lane, uint32_t t_row, uint32_t land,
-                                               uint32_t fold_bar, const volatile int *abort_flag) {
-    const long long tile_end = static_cast<long long>(w.tile - s.dp_tiles + 1) * s.kb;
-    const int q0 = s.sk_index + 1;
-    int q_end = q0;
-    while (q_end < s.sk_pairs && s.sk_begin(q_end) < tile_end) ++q_end;
-    const int nq = q_end - q0;
-    if (nq <= 0) return true;
+// Reduce-scatter, step 2a: wait (bounded) until every other unit of the
+// pair's split tiles (at most 2 x 5 flags) has published.  Lane l polls flag
+// l, so each pass is one round trip for all of them; the warp barrier at the
+// end orders lane 0's later bulk loads after every lane's acquire.
+__device__ __forceinline__ bool sk_wait_others(const KParams &p, const PairSchedule &s, const SplitTile *t, int nt,
+                                               uint32_t rank, int g, int lane, const volatile int *abort_flag) {
+    const int *mine = nullptr;
+    int l = 0;
+    for (int u = 0; u < nt; ++u)
+        for (int i = 0; i < t[u].n; ++i) {
+            if (i == t[u].j) continue;
+            if (l == lane) mine = sk_flag(p, sk_slot(s, t[u].q0 + i, t[u].rel), rank, g);
+            ++l;
+        }
     const uint64_t t0 = global_timer_ns();
-    bool ok = true;
-    for (int q = q0; ok && q < q_end; ++q) {
-        const int *f = sk_flag(p, q, rank, g);
-        while (ld_acquire_gpu(f) < 1) {
-            if (*abort_flag || global_timer_ns() - t0 > p.timeout_ns) {
-                ok = false;
-                break;
-            }
-        }
+    for (;;) {
+        const bool here = mine == nullptr || ld_acquire_gpu(mine) >= 1;
+        if (__all_sync(0xffffffffu, here)) break;
+        if (__any_sync(0xffffffffu, *abort_flag != 0 || global_timer_ns() - t0 > p.timeout_ns)) return false;
     }
-    if (!__all_sync(0xffffffffu, ok)) return false;
-    const int per_round = kLandBoxes / nq < kSkBoxes ? kLandBoxes / nq : kSkBoxes;
-    uint32_t phase = 0;
+    __syncwarp();
+    return true;
+}
+
+__device__ __forceinline__ int sk_land_boxes(const SplitTile &t) { return (t.c_end - t.c_begin) / 32 * (t.n - 1); }
+
+// Step 2b: bulk-load the other units' boxes of the own columns of split
+// units [u0, u1) into `land` (the idle operand ring), add them in slot order
+// to this warp's accumulator rows in TMEM.  False when a load did not land
+// in time.
+__device__ __forceinline__ bool sk_land_and_add(const KParams &p, const PairSchedule &s, const SplitTile *t,
+                                                const uint32_t *t_row, int u0, int u1, uint32_t rank, int g,
+                                                int lane, uint32_t land, uint32_t fold_bar, uint32_t &phase,
+                                                const volatile int *abort_flag) {
+    int boxes = 0;
+    for (int u = u0; u < u1; ++u) boxes += sk_land_boxes(t[u]);
+    if (boxes == 0) return true;
+    if (boxes > kLandBoxes) return false;  // cannot happen: one unit lands <= 12 boxes
+    if (lane == 0) {
+        fence_proxy_async_global();  // the acquired flags come before these async-proxy reads
+        mbar_arrive_expect_tx(fold_bar, static_cast<uint32_t>(boxes * kStageBoxBytes));
+        int b = 0;
+        for (int u = u0; u < u1; ++u)
+            for (int c = t[u].c_begin / 32; c < t[u].c_end / 32; ++c)
+                for (int i = 0; i < t[u].n; ++i) {
+                    if (i == t[u].j) continue;
+                    bulk_load(land + static_cast<uint32_t>(b++ * kStageBoxBytes),
+                              sk_box(p, sk_slot(s, t[u].q0 + i, t[u].rel), rank, g, c), kStageBoxBytes, fold_bar);
+                }
+    }
+    const bool landed = mbar_wait(fold_bar, phase, abort_flag, p.timeout_ns);
+    if (!__all_sync(0xffffffffu, landed)) return false;
+    phase ^= 1u;
+    int b = 0;
+    for (int u = u0; u < u1; ++u) {
+        const int others = t[u].n - 1;
 #pragma unroll 1
-    for (int c0 = 0; c0 < kSkBoxes; c0 += per_round) {
-        const int cn = kSkBoxes - c0 < per_round ? kSkBoxes - c0 : per_round;
-        if (lane == 0) {
-            fence_proxy_async_global();  // the acquired flags come before these async-proxy reads
-            mbar_arrive_expect_tx(fold_bar, static_cast<uint32_t>(cn * nq * kStageBoxBytes));
-            for (int i = 0; i < cn; ++i)
-                for (int j = 0; j < nq; ++j)
-                    bulk_load(land + static_cast<uint32_t>((i * nq + j) * kStageBoxBytes),
-                              sk_box(p, q0 + j, rank, g, c0 + i), kStageBoxBytes, fold_bar);
-        }
-        const bool landed = mbar_wait(fold_bar, phase, abort_flag, p.timeout_ns);
-        if (!__all_sync(0xffffffffu, landed)) return false;
-        phase ^= 1u;
-#pragma unroll 1
-        for (int i = 0; i < cn; ++i) {
+        for (int c = t[u].c_begin / 32; c < t[u].c_end / 32; ++c) {
             uint32_t r[32];
-            tmem_load_32(t_row + static_cast<uint32_t>((c0 + i) * 32), r);
+            tmem_load_32(t_row[u] + static_cast<uint32_t>(c * 32), r);
             tmem_load_wait();
-            for (int j = 0; j < nq; ++j) {
+            for (int o = 0; o < others; ++o, ++b) {
                 uint32_t v[32];
-                box_get_row(land + static_cast<uint32_t>((i * nq + j) * kStageBoxBytes), lane, v);
+                box_get_row(land + static_cast<uint32_t>(b * kStageBoxBytes), lane, v);
 #pragma unroll
-                for (int k = 0; k < 32; ++k) r[k] = __float_as_uint(__fadd_rn(__uint_as_float(r[k]), __uint_as_float(v[k])));
+                for (int k = 0; k < 32; ++k)
+                    r[k] = __float_as_uint(__fadd_rn(__uint_as_float(r[k]), __uint_as_float(v[k])));
             }
-            tmem_store_32(t_row + static_cast<uint32_t>((c0 + i) * 32), r);
+            tmem_store_32(t_row[u] + static_cast<uint32_t>(c * 32), r);
         }
-        fence_proxy_async_smem();  // these reads come before the next round's bulk writes
-        __syncwarp();
     }
     tmem_store_wait();
+    fence_proxy_async_smem();  // these reads come before any later bulk write into the landing slice
     __syncwarp();
-    if (lane == 0)
-        for (int q = q0; q < q_end; ++q) atomicSub(sk_flag(p, q, rank, g), 1);
     return true;
+}
+
+// Step 2c: one reader count off each flag this warp read.
+__device__ __forceinline__ void sk_release_reads(const KParams &p, const PairSchedule &s, const SplitTile *t, int nt,
+                                                 uint32_t rank, int g, int lane) {
+    if (lane != 0) return;
+    for (int u = 0; u < nt; ++u)
+        for (int i = 0; i < t[u].n; ++i)
+            if (i != t[u].j) atomicSub(sk_flag(p, sk_slot(s, t[u].q0 + i, t[u].rel), rank, g), 1);
 }
 
 struct PairCfg {
@@ -945,17 +1011,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         int sbuf = 0;
         const uint32_t even_tempty0 = map_to_rank(tempty_bar(0), 0);
         const uint32_t odd_tfull0 = map_to_rank(tfull_bar(0), 1);
-        // one unit: idx is its position in MMA order (accumulator idx & 1);
-        // ring_free: every MMA of the pair has completed (an owner's fold lands
-        // its pieces in the operand ring)
-        auto epilogue_unit = [&](const PairWork &u, int idx, bool ring_free) -> bool {
+        // the accumulator of the unit at MMA position idx (buffer idx & 1) is
+        // complete: wait for it and forward the news to the odd CTA
+        auto wait_full = [&](int idx) -> bool {
             const int acc = idx & 1;
-            const uint32_t acc_ph = static_cast<uint32_t>(idx >> 1) & 1u;
-            int64_t tm, tn;
-            tile_raster(num_m_pairs, num_n_pairs, kGroupM, u.tile, tm, tn);
-            const int m0 = static_cast<int>(tm) * 2 * kBlockM + static_cast<int>(rank) * kBlockM;
-            const int n0 = static_cast<int>(tn) * kPairN;
-            const bool ready = mbar_wait(tfull_bar(acc), acc_ph, abort_flag, p.timeout_ns);
+            const bool ready = mbar_wait(tfull_bar(acc), static_cast<uint32_t>(idx >> 1) & 1u, abort_flag, p.timeout_ns);
             if (!__all_sync(0xffffffffu, ready)) {
                 *abort_flag = 1;
                 if (lane == 0) atomicExch(p.err, kDevAbortGemmEpilogue);
@@ -963,25 +1023,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             }
             if (even && warp == 2 && lane == 0) mbar_arrive_cluster(odd_tfull0 + 8u * acc);
             tc_fence_after_sync();
-            const int row = m0 + g * 32 + lane;
-            const uint32_t t_row =
-                tmem_base + (static_cast<uint32_t>(g * 32) << 16) + static_cast<uint32_t>(acc * kPairN);
-            if (u.kind == kUnitOwner &&
-                (!ring_free ||
-                 !sk_fold_pieces(p, sched, u, rank, g, lane, t_row,
-                                 smem_addr(smem) + static_cast<uint32_t>(g * kLandBoxes * kStageBoxBytes), fold_bar(g),
-                                 abort_flag))) {
-                *abort_flag = 1;
-                if (lane == 0) atomicExch(p.err, kDevAbortGemmStreamK);
-                return false;
-            }
-            if (u.kind == kUnitPiece) {
-                sk_store_piece(p, sched.sk_index, rank, g, lane, t_row, staging, sbuf);
-            } else if (p.staged) {
-                store_tile_staged<kPairN>(p, cmaps, t_row, m0 + g * 32, n0, staging, sbuf, lane);
+            return true;
+        };
+        auto t_row_of = [&](int idx) {
+            return tmem_base + (static_cast<uint32_t>(g * 32) << 16) + static_cast<uint32_t>((idx & 1) * kPairN);
+        };
+        // bias, conversion and the store of accumulator columns [c_begin, c_end)
+        auto store_c = [&](const PairWork &u, int idx, int c_begin, int c_end) {
+            int64_t tm, tn;
+            tile_raster(num_m_pairs, num_n_pairs, kGroupM, u.tile, tm, tn);
+            const int m0 = static_cast<int>(tm) * 2 * kBlockM + static_cast<int>(rank) * kBlockM;
+            const int n0 = static_cast<int>(tn) * kPairN;
+            const uint32_t t_row = t_row_of(idx);
+            if (p.staged) {
+                store_tile_staged<kPairN>(p, cmaps, t_row, m0 + g * 32, n0, staging, sbuf, lane, c_begin, c_end);
             } else {
+                const int row = m0 + g * 32 + lane;
 #pragma unroll 1
-                for (int c = 0; c < kPairN / 32; ++c) {
+                for (int c = c_begin / 32; c < c_end / 32; ++c) {
                     const int col0 = n0 + c * 32;
                     if (col0 >= p.n) break;
                     uint32_t r[32];
@@ -991,31 +1050,71 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     if (row < p.m) store_row_chunk(p, row, col0, r);
                 }
             }
+        };
+        auto release = [&](int idx) {
             tc_fence_before_sync();
             __syncwarp();
             if (lane == 0) {
-                if (even) mbar_arrive(tempty_bar(acc));
-                else mbar_arrive_cluster(even_tempty0 + 8u * acc);
+                if (even) mbar_arrive(tempty_bar(idx & 1));
+                else mbar_arrive_cluster(even_tempty0 + 8u * (idx & 1));
             }
-            return true;
         };
+        // whole tiles in MMA order; a split tile's unit first publishes the
+        // columns the tile's other units own (no waiting) and keeps its
+        // accumulator.  Split units are the pair's last (at most two), so
+        // once all have published, every MMA of the pair is complete and the
+        // operand ring is free to land the other units' columns of its own.
         PairUnits units;
         units.init(sched, pair);
-        PairWork cur, nxt;
-        int idx = 0;
-        bool have_cur = units.next(sched, cur);
-        while (have_cur) {
-            const bool have_nxt = units.next(sched, nxt);
-            if (cur.kind == kUnitOwner && have_nxt) {
-                // the piece after an owned part is the pair's last MMA unit and
-                // another pair's owner waits for it: store it first
-                if (!epilogue_unit(nxt, idx + 1, false) || !epilogue_unit(cur, idx, true)) break;
+        PairWork w;
+        PairWork split_u0{}, split_u1{};
+        int n_split = 0, idx = 0;
+        bool ok = true;
+        for (; ok && units.next(sched, w); ++idx) {
+            if (!wait_full(idx)) {
+                ok = false;
                 break;
             }
-            if (!epilogue_unit(cur, idx, !have_nxt)) break;
-            ++idx;
-            cur = nxt;
-            have_cur = have_nxt;
+            if (w.kind == kUnitWhole) {
+                store_c(w, idx, 0, kPairN);
+                release(idx);
+                continue;
+            }
+            sk_publish(p, sched, split_tile(p, sched, w), rank, g, lane, t_row_of(idx), staging, sbuf);
+            if (n_split == 0) split_u0 = w;
+            else split_u1 = w;
+            ++n_split;
+        }
+        if (ok && n_split > 0) {
+            SplitTile st[2];
+            uint32_t rows[2];
+            for (int i = 0; i < n_split; ++i) {
+                st[i] = split_tile(p, sched, i == 0 ? split_u0 : split_u1);
+                rows[i] = t_row_of(idx - n_split + i);
+            }
+            uint32_t land_phase = 0;
+            const uint32_t land = smem_addr(smem) + static_cast<uint32_t>(g * kLandBoxes * kStageBoxBytes);
+            // both units' boxes in one round when they fit the landing slice
+            const bool one_round = n_split == 1 || sk_land_boxes(st[0]) + sk_land_boxes(st[1]) <= kLandBoxes;
+            bool folded = sk_wait_others(p, sched, st, n_split, rank, g, lane, abort_flag);
+            if (folded && one_round) {
+                folded = sk_land_and_add(p, sched, st, rows, 0, n_split, rank, g, lane, land, fold_bar(g), land_phase,
+                                         abort_flag);
+            } else {
+                for (int i = 0; folded && i < n_split; ++i)
+                    folded = sk_land_and_add(p, sched, st, rows, i, i + 1, rank, g, lane, land, fold_bar(g),
+                                             land_phase, abort_flag);
+            }
+            if (!folded) {
+                *abort_flag = 1;
+                if (lane == 0) atomicExch(p.err, kDevAbortGemmStreamK);
+            } else {
+                sk_release_reads(p, sched, st, n_split, rank, g, lane);
+                for (int i = 0; i < n_split; ++i) {
+                    store_c(i == 0 ? split_u0 : split_u1, idx - n_split + i, st[i].c_begin, st[i].c_end);
+                    release(idx - n_split + i);
+                }
+            }
         }
         if (p.staged && lane == 0) bulk_wait_group_all();  // every TMA store of C has landed
     }
@@ -1539,6 +1638,7 @@ int launch_gemm_3xtf32(const GemmArgs &g, int sm_count, int *dev_err, uint64_t t
     kp.c = g.c;
     kp.sk_ws = nullptr;
     kp.sk_flags = nullptr;
+    kp.sk_mode = 0;
     kp.staged = 0;  // direct stores
     kp.n_peers = g.peers.n;
     for (int i = 0; i < kMaxPeers; ++i) kp.c_peers[i] = i < g.peers.n ? g.peers.base[i] : nullptr;
@@ -1553,21 +1653,26 @@ int launch_gemm_3xtf32(const GemmArgs &g, int sm_count, int *dev_err, uint64_t t
     return launch_x3_instance<false, 64>(ma, mb, kp, plan.ctas, stream);
 }
 
-// SPTILES_B200_STREAM_K=0 turns the stream-K tail of the CTA-pair kernel off
-// (whole tiles only); on by default.
-bool stream_k_enabled() {
+// Stream-K mode of the CTA-pair kernel (stream_k_split): SPTILES_B200_STREAM_K
+// = 0 whole tiles only, 2 also partial last waves; 1 (default) only problems
+// with fewer tiles than pairs.
+int stream_k_mode() {
     const char *v = std::getenv("SPTILES_B200_STREAM_K");
-    return !(v != nullptr && v[0] == '0');
+    if (v != nullptr && v[0] == '0') return 0;
+    if (v != nullptr && v[0] == '2') return 2;
+    return 1;
 }
 
+// two slots per pair (a stream-K range covers at most two tiles), each with
+// both CTAs' 128 x 256 fp32 and a flag per epilogue warp and CTA
 size_t stream_k_flag_offset(int sm_count) {
     const int pairs = (sm_count > 0 ? sm_count : 148) / 2;
-    return static_cast<size_t>(pairs) * 2 * kPairN * kBlockM * sizeof(float);
+    return static_cast<size_t>(pairs) * 2 * 2 * kPairN * kBlockM * sizeof(float);
 }
 
 size_t stream_k_workspace_bytes(int sm_count) {
     const int pairs = (sm_count > 0 ? sm_count : 148) / 2;
-    return stream_k_flag_offset(sm_count) + static_cast<size_t>(pairs) * 2 * kEpilogueWarps * sizeof(int);
+    return stream_k_flag_offset(sm_count) + static_cast<size_t>(pairs) * 2 * 2 * kEpilogueWarps * sizeof(int);
 }
 
 int plan_gemm(int in_dtype, int64_t m, int64_t n, int64_t k, int sm_count, GemmPlan *plan) {
@@ -1611,7 +1716,7 @@ int plan_gemm(int in_dtype, int64_t m, int64_t n, int64_t k, int sm_count, GemmP
         int dp_tiles = 0, sk_pairs = 0;
         long long sk_iters = 0;
         if (tiles < (int64_t(1) << 30))
-            stream_k_split(static_cast<int>(tiles), pairs, kb, stream_k_enabled(), dp_tiles, sk_pairs, sk_iters);
+            stream_k_split(static_cast<int>(tiles), pairs, kb, stream_k_mode(), dp_tiles, sk_pairs, sk_iters);
         if (sk_pairs > 0) {
             // per pair: whole tiles, its tail range, ~6 K blocks of partial store / fold
             const double work = static_cast<double>(dp_tiles / pairs) * kb +
@@ -1639,7 +1744,7 @@ int plan_gemm(int in_dtype, int64_t m, int64_t n, int64_t k, int sm_count, GemmP
         int pairs = best.tiles < sm_count / 2 ? best.tiles : sm_count / 2;
         int dp_tiles = 0, sk_pairs = 0;
         long long sk_iters = 0;
-        stream_k_split(best.tiles, sm_count / 2, static_cast<int>(cdiv(k, best.block_k)), stream_k_enabled(),
+        stream_k_split(best.tiles, sm_count / 2, static_cast<int>(cdiv(k, best.block_k)), stream_k_mode(),
                        dp_tiles, sk_pairs, sk_iters);
         if (sk_pairs > 0) pairs = dp_tiles > 0 ? sm_count / 2 : sk_pairs;
         best.ctas = 2 * pairs;
@@ -1713,7 +1818,8 @@ int launch_gemm(const GemmArgs &g, int sm_count, int *dev_err, uint64_t timeout_
     kp.bias_dtype = g.bias_dtype;
     kp.err = dev_err;
     kp.timeout_ns = timeout_ns;
-    kp.sk_ws = plan.pair && stream_k_enabled() ? g.sk_ws : nullptr;
+    kp.sk_mode = stream_k_mode();
+    kp.sk_ws = plan.pair && kp.sk_mode > 0 ? g.sk_ws : nullptr;
     kp.sk_flags = kp.sk_ws ? g.sk_flags : nullptr;
     CStoreMaps cm;
     std::memset(&cm, 0, sizeof(cm));
@@ -1767,7 +1873,7 @@ extern "C" int st_stream_k_split(int32_t tiles, int32_t pairs, int32_t k_blocks,
         return st::fail(ST_ERR_INVALID_ARGUMENT, "st_stream_k_split: tiles >= 0, pairs and k_blocks > 0");
     int dp = 0, skp = 0;
     long long ski = 0;
-    st::stream_k_split(tiles, pairs, k_blocks, st::stream_k_enabled(), dp, skp, ski);
+    st::stream_k_split(tiles, pairs, k_blocks, st::stream_k_mode(), dp, skp, ski);
     *dp_tiles = dp;
     *sk_pairs = skp;
     *sk_iters = ski;
