@@ -359,34 +359,45 @@ def run_matmul(wl, args, rank, world, local, dist_on, peaks):
 
 
 def e2e_matmul(wl, args, a, b, bias, out_dt, rows, dist_on):
-    """Same metric through the public API on pinned host buffers (copies in the timed region)."""
+    """Same metric through the public API on pinned host buffers (copies in the timed region).
+
+    One GPU: sptiles_b200.matmul on host tensors (st_matmul_host).  N GPUs:
+    partition.sharded_matmul_host on each rank (its rows of A, 1/N of B's
+    rows copied and all-gathered over NVLink, its rows of C back).  Byte
+    counts are the whole job's per step."""
     import torch
     import sptiles_b200 as st
+    from sptiles_b200.partition import sharded_matmul_host
     ha = a.cpu().pin_memory()
     hb = b.cpu().pin_memory()
     hbias = bias.cpu().pin_memory() if bias is not None else None
     hc = torch.empty((rows, wl["n"]), dtype=out_dt).pin_memory()
     steps = max(1, min(args.steps, 10))
+
+    def step():
+        if dist_on:
+            sharded_matmul_host(ha, hb, hbias, m_total=wl["m"], out=hc)
+        elif rows:
+            st.matmul(ha, hb, hbias, out=hc)  # returns once C is back in host memory
     for _ in range(2):
-        if rows:
-            st.matmul(ha, hb, hbias, out=hc)
+        step()
     if dist_on:
         import torch.distributed as dist
         dist.barrier()
     t0 = time.perf_counter()
     for _ in range(steps):
-        if rows:
-            st.matmul(ha, hb, hbias, out=hc)  # returns once C is back in host memory
+        step()
     dt = time.perf_counter() - t0
     dt = max_over_ranks(dt, dist_on)
     total_flops = sum_over_ranks(flops_of(wl, rows), dist_on)
-    h2d = ha.numel() * ha.element_size() + hb.numel() * hb.element_size() + \
-        (hbias.numel() * hbias.element_size() if hbias is not None else 0)
-    d2h = hc.numel() * hc.element_size()
+    h2d = sum_over_ranks(ha.numel() * ha.element_size() + (hbias.numel() * hbias.element_size() if hbias is not None
+                                                           else 0), dist_on) + hb.numel() * hb.element_size()
+    d2h = sum_over_ranks(hc.numel() * hc.element_size(), dist_on)
+    how = ("partition.sharded_matmul_host on each rank: its rows of A and 1/N of B's rows H2D, B all-gathered "
+           "over NCCL, GEMM, its rows of C D2H" if dist_on else
+           "sptiles_b200.matmul on pinned host tensors (st_matmul_host): H2D, kernel, D2H")
     return {"value": round(total_flops * steps / dt / 1e12, 3), "unit": "TFLOP/s", "h2d_bytes_per_step": int(h2d),
-            "d2h_bytes_per_step": int(d2h), "steps": steps,
-            "how": "sptiles_b200.matmul on pinned host tensors (st_matmul_host): H2D, kernel, D2H per step, "
-                   "host wall clock"}
+            "d2h_bytes_per_step": int(d2h), "steps": steps, "how": how + " per step, host wall clock"}
 
 
 def vector_add_sweep(dev, peaks, exps=(20, 22, 24, 26, 28)):

@@ -188,3 +188,74 @@ class ReplicatedOutput:
         self._N.lib().st_free(self._ctx, self.device, self._ptr)
         self._ptr = None
         self._peers = []
+
+
+def sharded_matmul_host(a_local: torch.Tensor, b: torch.Tensor, bias: torch.Tensor | None = None, *, m_total: int,
+                        out: torch.Tensor | None = None, out_dtype: torch.dtype | None = None, group=None,
+                        chunk_bytes: int = 16 << 20) -> torch.Tensor:
+    """This rank's rows of C = A @ B (+ bias) with every operand in host memory.
+
+    ``a_local`` (this rank's rows of A), ``b``, ``bias`` and ``out`` are CPU
+    tensors, pinned for overlapped copies.  B is needed whole on every GPU but
+    crosses the host link once per job: each rank copies 1/N of B's rows to
+    its GPU and the slices are all-gathered over the process group (NCCL over
+    NVLink).  Meanwhile A comes in ~16 MB row chunks on a copy stream, each
+    chunk's GEMM runs once B is complete, and its rows of C go back on a
+    third stream.  Returns ``out`` (allocated if not given) once it holds the
+    result.
+    """
+    from .api import matmul
+
+    if a_local.is_cuda or b.is_cuda or (out is not None and out.is_cuda):
+        raise ValueError("sharded_matmul_host takes host tensors")
+    rank, ws = dist.get_rank(group), dist.get_world_size(group)
+    r0, r1 = matmul_row_shard(m_total, ws, rank)
+    if a_local.shape[0] != r1 - r0:
+        raise ValueError(f"rank {rank} holds {a_local.shape[0]} rows, its shard has {r1 - r0}")
+    k, n = b.shape
+    if a_local.shape[1] != k:
+        raise ValueError(f"A has {a_local.shape[1]} columns, B has {k} rows")
+    out_dtype = out_dtype or (out.dtype if out is not None else a_local.dtype)
+    if out is None:
+        out = torch.empty((a_local.shape[0], n), dtype=out_dtype, pin_memory=True)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    main = torch.cuda.current_stream(dev)
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    s_in.wait_stream(main)
+    s_out.wait_stream(main)
+    ks = -(-k // ws)  # B rows per rank (the last slices may be short or empty)
+    b_dev = torch.empty((ks * ws, n), dtype=b.dtype, device=dev)
+    rows = a_local.shape[0]
+    a_dev = torch.empty((rows, k), dtype=a_local.dtype, device=dev)
+    c_dev = torch.empty((rows, n), dtype=out_dtype, device=dev)
+    chunk = max(256, (chunk_bytes // max(1, k * a_local.element_size())) // 256 * 256)
+    with torch.cuda.stream(s_in):
+        k0, k1 = min(k, rank * ks), min(k, (rank + 1) * ks)
+        mine = b_dev[rank * ks:(rank + 1) * ks]
+        if k1 > k0:
+            mine[:k1 - k0].copy_(b[k0:k1], non_blocking=True)
+        if k1 - k0 < ks:
+            mine[max(0, k1 - k0):].zero_()
+        bias_dev = bias.to(dev, non_blocking=True) if bias is not None else None
+        b_ready = torch.cuda.Event()
+        b_ready.record(s_in)
+        a_ready = []
+        for c0 in range(0, rows, chunk):
+            a_dev[c0:c0 + chunk].copy_(a_local[c0:c0 + chunk], non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(s_in)
+            a_ready.append(ev)
+    main.wait_event(b_ready)  # this rank's slice of B and the bias are on the GPU
+    dist.all_gather_into_tensor(b_dev, mine, group=group)
+    b_full = b_dev[:k]
+    for i, c0 in enumerate(range(0, rows, chunk)):
+        main.wait_event(a_ready[i])
+        matmul(a_dev[c0:c0 + chunk], b_full, bias_dev, out=c_dev[c0:c0 + chunk])
+        done = torch.cuda.Event()
+        done.record(main)
+        s_out.wait_event(done)
+        with torch.cuda.stream(s_out):
+            out[c0:c0 + chunk].copy_(c_dev[c0:c0 + chunk], non_blocking=True)
+    main.wait_stream(s_out)
+    main.synchronize()
+    return out

@@ -72,6 +72,20 @@ def _worker(rank, world, port, q):
                               replicate_output=True)
         out["fused_vs_nccl"] = torch.equal(C2, want)
         rep2.close()
+        # host operands: 1/N of B's rows per rank, all-gathered on the GPUs
+        from sptiles_b200.partition import sharded_matmul_host
+
+        hA = torch.from_numpy(a[r0:r1]).to(torch.bfloat16).pin_memory()
+        hB = torch.from_numpy(b).to(torch.bfloat16).pin_memory()
+        Ch = sharded_matmul_host(hA, hB, m_total=m, out_dtype=torch.float32)
+        out["host_kat"] = Ch.numpy().tobytes() == oracle.matmul_kat_expected(m, n, k)[r0:r1].tobytes()
+        m3, n3, k3 = 300, 200, 1001  # B rows split 501 + 500 (the last slice short and zero padded)
+        a3 = oracle.kat_values(m3 * k3, 17, 8, 0.25).reshape(m3, k3)
+        b3 = oracle.kat_values(k3 * n3, 13, 6, 0.5).reshape(k3, n3)
+        t0, t1 = matmul_row_shard(m3, world, rank)
+        C3 = sharded_matmul_host(torch.from_numpy(a3[t0:t1]).half().pin_memory(), torch.from_numpy(b3).half(),
+                                 m_total=m3, out_dtype=torch.float32)
+        out["host_kat_odd_k"] = C3.numpy().tobytes() == oracle.matmul_kat_expected(m3, n3, k3)[t0:t1].tobytes()
         q.put((rank, out))
     finally:
         dist.destroy_process_group()
