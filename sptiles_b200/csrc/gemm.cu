@@ -555,7 +555,7 @@ __device__ __forceinline__ uint64_t operand_l2_policy_b() {
 // neighbouring tiles of the raster for L2 reuse.  With fewer tiles than pairs
 // (T < P) that would leave P - T pairs idle; instead the T * KB K blocks are
 // split into equal contiguous ranges over S > T pairs (at least KB / 4 blocks
-// each, so a tile has at most ~5 pieces).  The split is written for a tail
+// each, so a tile has at most ~5 units).  The split is written for a tail
 // after whole-tile waves too (dp_tiles > 0).  A split tile's units finish
 // together and reduce-scatter: each publishes the output columns the others
 // own (fp32, without waiting), then waits for the others' parts of its own
@@ -608,8 +608,8 @@ struct PairSchedule {
 
 // A pair's units in MMA order.  A stream-K range is at most one tile long
 // (r < P tiles over P pairs, or at most 2 * (kb / 4) blocks each), so it is
-// one unit or two: the end of tile s (a piece) and the start of
-// tile s + 1 (owned).  The owned part goes first, so that every pair starts
+// one unit or two: the end of tile s and the start of tile s + 1.  The
+// start of tile s + 1 goes first, so that every pair starts
 // its range at K block 0 and ends it at the last K block: the pairs sweep
 // the tiles' K blocks together, which keeps A and B reads shared in L2.
 struct PairUnits {
@@ -634,7 +634,7 @@ struct PairUnits {
         if (sa == sb) {
             u0 = unit(sa, a, b);
             n = 1;
-        } else {  // sb == sa + 1: owned start of tile sb first, then the piece of tile sa
+        } else {  // sb == sa + 1: the start of tile sb first, then the end of tile sa
             u0 = unit(sb, sb * s.kb, b);
             u1 = unit(sa, a, sb * s.kb);
             n = 2;
@@ -653,8 +653,8 @@ struct PairUnits {
     }
 };
 
-// A stream-K piece in the workspace: per (slot q, CTA rank, epilogue warp g)
-// 8 boxes of 4 KB; box c holds accumulator columns [32c, 32c + 32) of the
+// A split unit's partial accumulator in the workspace: per (slot, CTA rank,
+// epilogue warp g) 8 boxes of 4 KB; box c holds accumulator columns [32c, 32c + 32) of the
 // warp's 32 rows in the staging layout (one 128-byte row per lane, 16-byte
 // chunk j of row l at position j ^ (l mod 8)).
 constexpr int kSkBoxes = 256 / 32;
