@@ -72,13 +72,27 @@ def gather_row_shards(local: torch.Tensor, m_total: int, *, group=None, out: tor
 
 def sharded_matmul(a_local: torch.Tensor, b: torch.Tensor, bias: torch.Tensor | None = None, *, m_total: int,
                    out_dtype: torch.dtype | None = None, replicate_output: bool = False, group=None) -> torch.Tensor:
-    """This rank's rows of C = A @ B (+ bias); the full C when ``replicate_output``."""
+    """This rank's rows of C = A @ B (+ bias); the full C when ``replicate_output``.
+
+    With equal shards the GEMM writes straight into this rank's rows of the
+    full C and the all-gather runs in place (each rank's send buffer is its
+    own slice of the receive buffer), so nothing is copied on the GPU.
+    """
     from .api import matmul
 
-    c_local = matmul(a_local, b, bias, out_dtype=out_dtype)
     if not replicate_output:
-        return c_local
-    return gather_row_shards(c_local, m_total, group=group)
+        return matmul(a_local, b, bias, out_dtype=out_dtype)
+    rank, ws = dist.get_rank(group), dist.get_world_size(group)
+    spans = [matmul_row_shard(m_total, ws, r) for r in range(ws)]
+    if len({e - b0 for b0, e in spans}) == 1 and a_local.shape[0] == spans[rank][1] - spans[rank][0]:
+        dt = out_dtype or a_local.dtype
+        full = torch.empty((m_total, b.shape[1]), dtype=dt, device=a_local.device)
+        r0, r1 = spans[rank]
+        mine = full[r0:r1]
+        matmul(a_local, b, bias, out=mine)
+        dist.all_gather_into_tensor(full, mine, group=group)
+        return full
+    return gather_row_shards(matmul(a_local, b, bias, out_dtype=out_dtype), m_total, group=group)
 
 
 def sharded_vector_add(a_local: torch.Tensor, b_local: torch.Tensor) -> torch.Tensor:
