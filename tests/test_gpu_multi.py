@@ -72,6 +72,22 @@ def _worker(rank, world, port, q):
                               replicate_output=True)
         out["fused_vs_nccl"] = torch.equal(C2, want)
         rep2.close()
+        # fp32 operands (packed 3xTF32; a few tiles per rank, so the stream-K
+        # split with peer copies) and a 16-bit replicated C
+        m4, n4, k4 = 1000, 520, 700
+        a4 = oracle.kat_values(m4 * k4, 17, 8, 0.25).reshape(m4, k4)
+        b4 = oracle.kat_values(k4 * n4, 13, 6, 0.5).reshape(k4, n4)
+        u0, u1 = matmul_row_shard(m4, world, rank)
+        rep4 = ReplicatedOutput(m4, n4, torch.float32)
+        C4 = rep4.matmul(torch.from_numpy(a4[u0:u1]).to(dev), torch.from_numpy(b4).to(dev))
+        out["fused_fp32_kat"] = C4.cpu().numpy().tobytes() == oracle.matmul_kat_expected(m4, n4, k4).tobytes()
+        rep4.close()
+        rep5 = ReplicatedOutput(m2, 768, torch.float16)
+        C5 = rep5.matmul(A2[s0:s1].to(dev).half(), B2.to(dev).half(), bias2.to(dev))
+        want5 = sharded_matmul(A2[s0:s1].to(dev).half(), B2.to(dev).half(), bias2.to(dev), m_total=m2,
+                               out_dtype=torch.float16, replicate_output=True)
+        out["fused_f16_out"] = torch.equal(C5, want5)
+        rep5.close()
         # host operands: 1/N of B's rows per rank, all-gathered on the GPUs
         from sptiles_b200.partition import sharded_matmul_host
 
