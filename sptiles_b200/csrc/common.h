@@ -6,6 +6,7 @@
 
 #include <cstdint>
 #include <string>
+#include <utility>
 
 #include "../../include/sptiles_b200.h"
 
@@ -29,6 +30,43 @@ int cuda_fail(cudaError_t e, const char *what);
     } while (0)
 
 inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+// ---- programmatic dependent launch
+// Every kernel of this library is launched with programmatic stream
+// serialisation (launch_kernel) and waits (pdl_wait) until the previous
+// kernel on the stream has completed and its memory is visible before it
+// touches global memory; only code before that -- barrier set-up, TMEM
+// allocation, tensor-map prefetch -- overlaps the predecessor.  pdl_trigger
+// lets the next kernel start launching: the GEMMs do it at once (one CTA per
+// SM, so a successor's CTAs only take SMs this grid has left), the streaming
+// kernels after their loop (their successors' CTAs would otherwise sit
+// resident beside them).  SPTILES_B200_PDL=0 launches without the attribute.
+#ifdef __CUDACC__
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_begin() {
+    pdl_trigger();
+    pdl_wait();
+}
+#endif
+
+bool pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_kernel(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                                 Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
 
 // Process-wide count of kernel launches issued by this library.
 void note_launch(uint64_t n = 1);
@@ -116,6 +154,7 @@ struct GemmArgs {
 // Partial accumulators (one 256 x 256 fp32 tile per CTA pair) and arrival
 // flags of the stream-K tail, for up to sm_count / 2 pairs.
 size_t stream_k_workspace_bytes(int sm_count);
+bool gemm_uses_stream_k(const GemmArgs &args, int sm_count);
 size_t stream_k_flag_offset(int sm_count);
 int launch_gemm(const GemmArgs &args, int sm_count, int *dev_err, uint64_t timeout_ns, cudaStream_t stream);
 // fp32 A and B used in place (TMA-addressable): the split into tf32 hi/lo

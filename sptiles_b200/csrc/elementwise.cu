@@ -33,6 +33,7 @@ int grid_for(int64_t items, int sm_count) {
 __global__ void __launch_bounds__(kThreads) fma_vec4_kernel(const float4 *__restrict__ a, const float4 *__restrict__ b,
                                                             const float4 *__restrict__ d, float4 *__restrict__ c,
                                                             int64_t n4) {
+    pdl_wait();
     const int64_t step = static_cast<int64_t>(gridDim.x) * kThreads;
     for (int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; i < n4; i += step) {
         const float4 x = __ldcs(a + i), y = __ldcs(b + i), z = __ldcs(d + i);
@@ -43,6 +44,7 @@ __global__ void __launch_bounds__(kThreads) fma_vec4_kernel(const float4 *__rest
         r.w = __fmaf_rn(x.w, y.w, z.w);
         __stcs(c + i, r);
     }
+    pdl_trigger();
 }
 
 struct View2 {
@@ -52,6 +54,7 @@ struct View2 {
 
 __global__ void __launch_bounds__(kThreads) fma_2d_kernel(View2 a, View2 b, View2 d, float *__restrict__ c, int64_t sc0,
                                                           int64_t sc1, int64_t rows, int64_t cols) {
+    pdl_wait();
     const int64_t total = rows * cols;
     const int64_t step = static_cast<int64_t>(gridDim.x) * kThreads;
     for (int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; i < total; i += step) {
@@ -61,6 +64,7 @@ __global__ void __launch_bounds__(kThreads) fma_2d_kernel(View2 a, View2 b, View
         const float z = static_cast<const float *>(d.p)[r * d.s0 + q * d.s1];
         c[r * sc0 + q * sc1] = __fmaf_rn(x, y, z);
     }
+    pdl_trigger();
 }
 
 // ------------------------------------------------------------------ cast
@@ -85,6 +89,7 @@ __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) { retu
 // Contiguous: four elements per thread per step (aligned to four elements).
 template <typename In, typename Out>
 __global__ void __launch_bounds__(kThreads) cast_vec4_kernel(const In *__restrict__ a, Out *__restrict__ c, int64_t n4) {
+    pdl_wait();
     struct alignas(4 * sizeof(In)) InVec { In v[4]; };
     struct alignas(4 * sizeof(Out)) OutVec { Out v[4]; };
     const InVec *av = reinterpret_cast<const InVec *>(a);
@@ -97,18 +102,21 @@ __global__ void __launch_bounds__(kThreads) cast_vec4_kernel(const In *__restric
         for (int j = 0; j < 4; ++j) y.v[j] = from_f32<Out>(to_f32<In>(x.v[j]));
         cv[i] = y;
     }
+    pdl_trigger();
 }
 
 template <typename In, typename Out>
 __global__ void __launch_bounds__(kThreads) cast_2d_kernel(const In *__restrict__ a, int64_t sa0, int64_t sa1,
                                                            Out *__restrict__ c, int64_t sc0, int64_t sc1, int64_t rows,
                                                            int64_t cols) {
+    pdl_wait();
     const int64_t total = rows * cols;
     const int64_t step = static_cast<int64_t>(gridDim.x) * kThreads;
     for (int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; i < total; i += step) {
         const int64_t r = i / cols, q = i - r * cols;
         c[r * sc0 + q * sc1] = from_f32<Out>(to_f32<In>(a[r * sa0 + q * sa1]));
     }
+    pdl_trigger();
 }
 
 template <typename In, typename Out>
@@ -122,17 +130,17 @@ int cast_typed(const void *a, const int64_t sa[2], void *c, const int64_t sc[2],
                          (reinterpret_cast<uintptr_t>(c) % (4 * sizeof(Out))) == 0;
     if (dense && aligned && n >= 4) {
         const int64_t n4 = n / 4;
-        cast_vec4_kernel<In, Out><<<grid_for(n4, sm_count), kThreads, 0, stream>>>(ap, cp, n4);
+        ST_CUDA_TRY(launch_kernel(cast_vec4_kernel<In, Out>, grid_for(n4, sm_count), kThreads, 0, stream, ap, cp, n4));
         note_launch();
         if (n4 * 4 < n) {
             const int64_t s1[2] = {0, 1};
-            cast_2d_kernel<In, Out><<<1, kThreads, 0, stream>>>(ap + n4 * 4, s1[0], s1[1], cp + n4 * 4, 0, 1, 1,
-                                                                n - n4 * 4);
+            ST_CUDA_TRY(launch_kernel(cast_2d_kernel<In, Out>, 1, kThreads, 0, stream, ap + n4 * 4, s1[0], s1[1],
+                                      cp + n4 * 4, 0, 1, 1, n - n4 * 4));
             note_launch();
         }
     } else {
-        cast_2d_kernel<In, Out><<<grid_for(n, sm_count), kThreads, 0, stream>>>(ap, sa[0], sa[1], cp, sc[0], sc[1],
-                                                                                 rows, cols);
+        ST_CUDA_TRY(launch_kernel(cast_2d_kernel<In, Out>, grid_for(n, sm_count), kThreads, 0, stream, ap, sa[0], sa[1],
+                                  cp, sc[0], sc[1], rows, cols));
         note_launch();
     }
     const cudaError_t e = cudaPeekAtLastError();
@@ -167,20 +175,19 @@ int launch_vector_fma(const float *a, const int64_t sa[2], const float *b, const
                          reinterpret_cast<uintptr_t>(d) % 16 == 0 && reinterpret_cast<uintptr_t>(c) % 16 == 0;
     if (dense && aligned && n >= 4) {
         const int64_t n4 = n / 4;
-        fma_vec4_kernel<<<grid_for(n4, sm_count), kThreads, 0, stream>>>(
-            reinterpret_cast<const float4 *>(a), reinterpret_cast<const float4 *>(b),
-            reinterpret_cast<const float4 *>(d), reinterpret_cast<float4 *>(c), n4);
+        ST_CUDA_TRY(launch_kernel(fma_vec4_kernel, grid_for(n4, sm_count), kThreads, 0, stream,
+                                  reinterpret_cast<const float4 *>(a), reinterpret_cast<const float4 *>(b),
+                                  reinterpret_cast<const float4 *>(d), reinterpret_cast<float4 *>(c), n4));
         note_launch();
         if (n4 * 4 < n) {
             const int64_t off = n4 * 4;
-            fma_2d_kernel<<<1, kThreads, 0, stream>>>(View2{a + off, 0, 1}, View2{b + off, 0, 1},
-                                                      View2{d + off, 0, 1}, c + off, 0, 1, 1, n - off);
+            ST_CUDA_TRY(launch_kernel(fma_2d_kernel, 1, kThreads, 0, stream, View2{a + off, 0, 1},
+                                      View2{b + off, 0, 1}, View2{d + off, 0, 1}, c + off, 0, 1, 1, n - off));
             note_launch();
         }
     } else {
-        fma_2d_kernel<<<grid_for(n, sm_count), kThreads, 0, stream>>>(View2{a, sa[0], sa[1]}, View2{b, sb[0], sb[1]},
-                                                                       View2{d, sd[0], sd[1]}, c, sc[0], sc[1], rows,
-                                                                       cols);
+        ST_CUDA_TRY(launch_kernel(fma_2d_kernel, grid_for(n, sm_count), kThreads, 0, stream, View2{a, sa[0], sa[1]},
+                                  View2{b, sb[0], sb[1]}, View2{d, sd[0], sd[1]}, c, sc[0], sc[1], rows, cols));
         note_launch();
     }
     const cudaError_t e = cudaPeekAtLastError();

@@ -336,6 +336,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after_sync();
     const uint32_t tmem_base = *tmem_slot;
+    pdl_begin();  // nothing above touches global memory
 
     if (warp == 0) {
         // ------------------------------------------------ TMA producer
@@ -894,6 +895,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     cluster_sync();  // barriers of both CTAs initialised, TMEM allocated
     tc_fence_after_sync();
     const uint32_t tmem_base = *tmem_slot;
+    pdl_begin();  // nothing above touches global memory
     const uint32_t even_full0 = map_to_rank(full_bar(0), 0);  // full[s] of the even CTA: + 8 s
 
     const int num_m_pairs = (p.m + 2 * kBlockM - 1) / (2 * kBlockM);
@@ -1223,6 +1225,7 @@ __global__ void __launch_bounds__(kX3Threads, 1)
     __syncthreads();
     tc_fence_after_sync();
     const uint32_t tmem_base = *tmem_slot;
+    pdl_begin();  // nothing above touches global memory
 
     if (warp == 0) {
         // ------------------------------------------------ TMA producer
@@ -1499,7 +1502,7 @@ int launch_instance(const CUtensorMap &ma, const CUtensorMap &mb, const KParams 
         ST_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
         if (dev >= 0 && dev < 64) attr_set |= 1ull << dev;
     }
-    kern<<<ctas, kThreads, Cfg::kSmemBytes, stream>>>(ma, mb, kp, cm);
+    ST_CUDA_TRY(launch_kernel(kern, ctas, kThreads, Cfg::kSmemBytes, stream, ma, mb, kp, cm));
     note_launch();
     const cudaError_t e = cudaPeekAtLastError();
     return e == cudaSuccess ? ST_OK : cuda_fail(cudaGetLastError(), "gemm_tc_kernel launch");
@@ -1552,7 +1555,7 @@ int launch_pair(const CUtensorMap &ma, const CUtensorMap &mb, const KParams &kp,
     if (std::getenv("SPTILES_B200_DEBUG"))
         std::fprintf(stderr, "[sptiles_b200] pair gemm: %d pairs (wanted %d, co-resident clusters %d), smem %d\n",
                      pairs, pairs_wanted, clusters, PairCfg::kSmemBytes);
-    kern<<<2 * pairs, kThreads, PairCfg::kSmemBytes, stream>>>(ma, mb, kp, cm);
+    ST_CUDA_TRY(launch_kernel(kern, 2 * pairs, kThreads, PairCfg::kSmemBytes, stream, ma, mb, kp, cm));
     note_launch();
     const cudaError_t e = cudaPeekAtLastError();
     return e == cudaSuccess ? ST_OK : cuda_fail(cudaGetLastError(), "gemm_tc_pair_kernel launch");
@@ -1570,7 +1573,7 @@ int launch_x3_instance(const CUtensorMap &ma, const CUtensorMap &mb, const KPara
         ST_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
         if (dev >= 0 && dev < 64) attr_set |= 1ull << dev;
     }
-    kern<<<ctas, kX3Threads, Cfg::kSmemBytes, stream>>>(ma, mb, kp);
+    ST_CUDA_TRY(launch_kernel(kern, ctas, kX3Threads, Cfg::kSmemBytes, stream, ma, mb, kp));
     note_launch();
     const cudaError_t e = cudaPeekAtLastError();
     return e == cudaSuccess ? ST_OK : cuda_fail(cudaGetLastError(), "gemm_tf32x3_kernel launch");
@@ -1762,6 +1765,21 @@ int plan_gemm(int in_dtype, int64_t m, int64_t n, int64_t k, int sm_count, GemmP
 // direct stores.  Peer copies always go by TMA store (one asynchronous bulk
 // store per box and destination instead of per-lane stores across NVLink);
 // a local C does unless SPTILES_B200_C_STORE=direct (or =tma) overrides it.
+// Whether launch_gemm would split tiles for these arguments (the stream-K
+// workspace is only acquired then, so other calls put no event between
+// their launches).
+bool gemm_uses_stream_k(const GemmArgs &g, int sm_count) {
+    const int mode = stream_k_mode();
+    if (mode <= 0) return false;
+    GemmPlan plan;
+    if (plan_gemm(g.ab_dtype, g.m, g.n, g.k, sm_count, &plan) != ST_OK || !plan.pair) return false;
+    if (sm_count <= 0) sm_count = 148;
+    int dp = 0, skp = 0;
+    long long ski = 0;
+    stream_k_split(plan.tiles, sm_count / 2, static_cast<int>(cdiv(g.k, plan.block_k)), mode, dp, skp, ski);
+    return skp > 0;
+}
+
 bool c_store_staged(const GemmArgs &g) {
     const int ces = dtype_size(g.c_dtype);
     if ((g.ldc * ces) % 16 != 0) return false;

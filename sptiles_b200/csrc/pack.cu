@@ -39,6 +39,7 @@ __device__ __forceinline__ float tf32_round(float x) {
 __global__ void __launch_bounds__(kThreads) pack_a_kernel(const float *__restrict__ a, int64_t sa0, int64_t sa1,
                                                           int64_t m, int64_t k, float *__restrict__ ap,
                                                           int64_t kp) {
+    pdl_wait();
     // one thread per 4 consecutive k of one row
     const int64_t groups = kp / 4;
     const int64_t total = m * groups;
@@ -59,12 +60,14 @@ __global__ void __launch_bounds__(kThreads) pack_a_kernel(const float *__restric
         row[(kp + k0) / 4] = h;
         row[(2 * kp + k0) / 4] = make_float4(lo[0], lo[1], lo[2], lo[3]);
     }
+    pdl_trigger();
 }
 
 // B [K, N] -> Bp [N, 3*kp]: 32 x 32 tiles transposed through shared memory.
 __global__ void __launch_bounds__(kThreads) pack_b_kernel(const float *__restrict__ b, int64_t sb0, int64_t sb1,
                                                           int64_t k, int64_t n, float *__restrict__ bp,
                                                           int64_t kp) {
+    pdl_wait();
     __shared__ float hi_t[32][33];
     __shared__ float lo_t[32][33];
     const int64_t k0 = static_cast<int64_t>(blockIdx.x) * 32;
@@ -88,6 +91,7 @@ __global__ void __launch_bounds__(kThreads) pack_b_kernel(const float *__restric
             row[2 * kp + kk] = h;
         }
     }
+    pdl_trigger();
 }
 
 // Both operands in one launch: blocks [0, tiles_b) transpose B's 32 x 32
@@ -97,6 +101,7 @@ __global__ void __launch_bounds__(kThreads) pack_ab_kernel(const float *__restri
                                                            int64_t sb1, int64_t n, int64_t k, int64_t kp,
                                                            float *__restrict__ ap, float *__restrict__ bp,
                                                            int tiles_k, int tiles_b) {
+    pdl_wait();
     __shared__ float hi_t[32][33];
     __shared__ float lo_t[32][33];
     if (static_cast<int>(blockIdx.x) < tiles_b) {
@@ -142,17 +147,20 @@ __global__ void __launch_bounds__(kThreads) pack_ab_kernel(const float *__restri
         row[(kp + k0) / 4] = h;
         row[(2 * kp + k0) / 4] = make_float4(lo[0], lo[1], lo[2], lo[3]);
     }
+    pdl_trigger();
 }
 
 __global__ void __launch_bounds__(kThreads) repack_16_kernel(const uint16_t *__restrict__ src, int64_t s0,
                                                              int64_t s1, int64_t rows, int64_t cols,
                                                              uint16_t *__restrict__ dst, int64_t ld) {
+    pdl_wait();
     const int64_t total = rows * ld;
     const int64_t step = static_cast<int64_t>(gridDim.x) * kThreads;
     for (int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; i < total; i += step) {
         const int64_t r = i / ld, c = i - r * ld;
         dst[i] = c < cols ? src[r * s0 + c * s1] : static_cast<uint16_t>(0);
     }
+    pdl_trigger();
 }
 
 int grid_1d(int64_t items) {
@@ -168,7 +176,7 @@ int64_t tf32_packed_k(int64_t k) { return cdiv(k, 32) * 32; }
 int launch_pack_a_tf32(const float *a, int64_t sa0, int64_t sa1, int64_t m, int64_t k, float *ap, int64_t kp,
                        cudaStream_t stream) {
     if (m <= 0 || kp <= 0) return ST_OK;
-    pack_a_kernel<<<grid_1d(m * (kp / 4)), kThreads, 0, stream>>>(a, sa0, sa1, m, k, ap, kp);
+    ST_CUDA_TRY(launch_kernel(pack_a_kernel, grid_1d(m * (kp / 4)), kThreads, 0, stream, a, sa0, sa1, m, k, ap, kp));
     note_launch();
     const cudaError_t e = cudaPeekAtLastError();
     return e == cudaSuccess ? ST_OK : cuda_fail(cudaGetLastError(), "pack_a_kernel");
@@ -178,7 +186,7 @@ int launch_pack_b_tf32(const float *b, int64_t sb0, int64_t sb1, int64_t k, int6
                        cudaStream_t stream) {
     if (n <= 0 || kp <= 0) return ST_OK;
     dim3 grid(static_cast<unsigned>(cdiv(kp, 32)), static_cast<unsigned>(cdiv(n, 32)));
-    pack_b_kernel<<<grid, kThreads, 0, stream>>>(b, sb0, sb1, k, n, bp, kp);
+    ST_CUDA_TRY(launch_kernel(pack_b_kernel, grid, kThreads, 0, stream, b, sb0, sb1, k, n, bp, kp));
     note_launch();
     const cudaError_t e = cudaPeekAtLastError();
     return e == cudaSuccess ? ST_OK : cuda_fail(cudaGetLastError(), "pack_b_kernel");
@@ -192,9 +200,9 @@ int launch_pack_ab_tf32(const float *a, int64_t sa0, int64_t sa1, int64_t m, con
     const int64_t blocks_a = m > 0 ? grid_1d(m * (kp / 4)) : 0;
     if (tiles_b + blocks_a > (int64_t(1) << 31) - 1)
         return fail(ST_ERR_UNSUPPORTED, "fp32 operands too large for one pack launch");
-    pack_ab_kernel<<<static_cast<unsigned>(tiles_b + blocks_a), kThreads, 0, stream>>>(
-        a, sa0, sa1, blocks_a > 0 ? m : 0, b, sb0, sb1, n, k, kp, ap, bp, static_cast<int>(tiles_k),
-        static_cast<int>(tiles_b));
+    ST_CUDA_TRY(launch_kernel(pack_ab_kernel, static_cast<unsigned>(tiles_b + blocks_a), kThreads, 0, stream, a, sa0,
+                              sa1, blocks_a > 0 ? m : 0, b, sb0, sb1, n, k, kp, ap, bp, static_cast<int>(tiles_k),
+                              static_cast<int>(tiles_b)));
     note_launch();
     const cudaError_t e = cudaPeekAtLastError();
     return e == cudaSuccess ? ST_OK : cuda_fail(cudaGetLastError(), "pack_ab_kernel");
@@ -203,7 +211,8 @@ int launch_pack_ab_tf32(const float *a, int64_t sa0, int64_t sa1, int64_t m, con
 int launch_repack_16(const uint16_t *src, int64_t s0, int64_t s1, int64_t rows, int64_t cols, uint16_t *dst,
                      int64_t ld, cudaStream_t stream) {
     if (rows <= 0 || ld <= 0) return ST_OK;
-    repack_16_kernel<<<grid_1d(rows * ld), kThreads, 0, stream>>>(src, s0, s1, rows, cols, dst, ld);
+    ST_CUDA_TRY(
+        launch_kernel(repack_16_kernel, grid_1d(rows * ld), kThreads, 0, stream, src, s0, s1, rows, cols, dst, ld));
     note_launch();
     const cudaError_t e = cudaPeekAtLastError();
     return e == cudaSuccess ? ST_OK : cuda_fail(cudaGetLastError(), "repack_16_kernel");

@@ -31,6 +31,14 @@ static std::atomic<uint64_t> g_launches{0};
 
 void note_launch(uint64_t n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
 
+bool pdl_enabled() {
+    static const bool on = [] {
+        const char *v = std::getenv("SPTILES_B200_PDL");
+        return !(v != nullptr && v[0] == '0');
+    }();
+    return on;
+}
+
 int fail(int code, const std::string &msg) {
     g_last_error = msg;
     return code;
@@ -319,6 +327,7 @@ int check_matmul(const st_tensor *a, const st_tensor *b, const st_tensor *bias, 
 
 __global__ void fill_rows_kernel(void *c, int64_t ldc, int c_dtype, const void *bias, int bias_dtype, int64_t m,
                                  int64_t n) {
+    pdl_wait();
     const int64_t total = m * n;
     for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
          i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -334,6 +343,7 @@ __global__ void fill_rows_kernel(void *c, int64_t ldc, int c_dtype, const void *
         else if (c_dtype == ST_F16) static_cast<__half *>(c)[r * ldc + q] = __float2half_rn(v);
         else static_cast<__nv_bfloat16 *>(c)[r * ldc + q] = __float2bfloat16_rn(v);
     }
+    pdl_trigger();
 }
 
 int matmul_device(const ExecCtx &x, const st_tensor &a, const st_tensor &b, const st_tensor *bias,
@@ -344,7 +354,8 @@ int matmul_device(const ExecCtx &x, const st_tensor &a, const st_tensor &b, cons
     const int bias_dtype = bias ? bias->dtype : ST_F32;
     if (K == 0) {  // empty contraction: C = 0 (+ bias)
         if (peers && peers->n > 0) return fail(ST_ERR_UNSUPPORTED, "K = 0 with peer outputs");
-        fill_rows_kernel<<<148, 256, 0, x.stream>>>(c.data, c.strides[0], c.dtype, bias_ptr, bias_dtype, M, N);
+        ST_CUDA_TRY(launch_kernel(fill_rows_kernel, 148, 256, 0, x.stream, c.data, c.strides[0], c.dtype, bias_ptr,
+                                  bias_dtype, M, N));
         note_launch();
         const cudaError_t e = cudaPeekAtLastError();
         return e == cudaSuccess ? ST_OK : cuda_fail(cudaGetLastError(), "fill_rows_kernel");
@@ -395,7 +406,7 @@ int matmul_device(const ExecCtx &x, const st_tensor &a, const st_tensor &b, cons
         g.ldb = 3 * kp;
         g.b_k_major = true;
         g.k = 3 * kp;
-        ST_TRY(sk_acquire(x.dev, x.stream, g));
+        if (gemm_uses_stream_k(g, x.dev->sm_count)) ST_TRY(sk_acquire(x.dev, x.stream, g));
         ST_TRY(launch_gemm(g, x.dev->sm_count, x.dev->dev_err, kDeviceWaitLimitNs, x.stream));
         if (g.sk_ws) ST_TRY(ws_release(x.dev->sk, x.stream));
         return ws_release(ws, x.stream);
@@ -440,7 +451,7 @@ int matmul_device(const ExecCtx &x, const st_tensor &a, const st_tensor &b, cons
         g.ldb = ldb_p;
         g.b_k_major = false;
     }
-    ST_TRY(sk_acquire(x.dev, x.stream, g));
+    if (gemm_uses_stream_k(g, x.dev->sm_count)) ST_TRY(sk_acquire(x.dev, x.stream, g));
     ST_TRY(launch_gemm(g, x.dev->sm_count, x.dev->dev_err, kDeviceWaitLimitNs, x.stream));
     if (g.sk_ws) ST_TRY(ws_release(x.dev->sk, x.stream));
     if (need) return ws_release(ws, x.stream);

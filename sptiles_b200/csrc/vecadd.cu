@@ -42,6 +42,7 @@ __device__ __forceinline__ void store_stream(float4 *p, float4 v) {
 __global__ void __launch_bounds__(kThreads) vadd_vec4_kernel(const float4 *__restrict__ a,
                                                              const float4 *__restrict__ b, float4 *__restrict__ c,
                                                              int64_t n4) {
+    pdl_wait();
     const int64_t step = static_cast<int64_t>(gridDim.x) * kThreads * kUnroll;
     int64_t base = static_cast<int64_t>(blockIdx.x) * kThreads * kUnroll + threadIdx.x;
     // full iterations: every unrolled slot is in range
@@ -76,15 +77,18 @@ __global__ void __launch_bounds__(kThreads) vadd_vec4_kernel(const float4 *__res
             store_stream(c + i, r);
         }
     }
+    pdl_trigger();
 }
 
 // Any element strides (also the misaligned head/tail of the vector path).
 __global__ void __launch_bounds__(kThreads) vadd_strided_kernel(const float *__restrict__ a, int64_t sa,
                                                                 const float *__restrict__ b, int64_t sb,
                                                                 float *__restrict__ c, int64_t sc, int64_t n) {
+    pdl_wait();
     const int64_t step = static_cast<int64_t>(gridDim.x) * kThreads;
     for (int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; i < n; i += step)
         c[i * sc] = a[i * sa] + b[i * sb];
+    pdl_trigger();
 }
 
 // 2D rectangle with arbitrary strides: rows x cols, one thread per element of
@@ -93,12 +97,14 @@ __global__ void __launch_bounds__(kThreads) vadd_2d_kernel(const float *__restri
                                                            const float *__restrict__ b, int64_t sb0, int64_t sb1,
                                                            float *__restrict__ c, int64_t sc0, int64_t sc1,
                                                            int64_t rows, int64_t cols) {
+    pdl_wait();
     const int64_t total = rows * cols;
     const int64_t step = static_cast<int64_t>(gridDim.x) * kThreads;
     for (int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; i < total; i += step) {
         const int64_t r = i / cols, q = i - r * cols;
         c[r * sc0 + q * sc1] = a[r * sa0 + q * sa1] + b[r * sb0 + q * sb1];
     }
+    pdl_trigger();
 }
 
 int grid_for(int64_t work_items, int per_cta, int sm_count) {
@@ -118,7 +124,8 @@ int launch_vector_add_1d(const float *a, int64_t sa, const float *b, int64_t sb,
     const bool unit = sa == 1 && sb == 1 && sc == 1;
     const bool same_phase = (pa % 16) == (pb % 16) && (pa % 16) == (pc % 16) && (pa % 4) == 0;
     if (!unit || !same_phase || n < 64) {
-        vadd_strided_kernel<<<grid_for(n, kThreads, sm_count), kThreads, 0, stream>>>(a, sa, b, sb, c, sc, n);
+        ST_CUDA_TRY(launch_kernel(vadd_strided_kernel, grid_for(n, kThreads, sm_count), kThreads, 0, stream, a, sa, b,
+                                  sb, c, sc, n));
         note_launch();
         return cudaPeekAtLastError() == cudaSuccess ? ST_OK : cuda_fail(cudaGetLastError(), "vadd_strided_kernel");
     }
@@ -127,18 +134,19 @@ int launch_vector_add_1d(const float *a, int64_t sa, const float *b, int64_t sb,
     const int64_t body4 = (n - head) / 4;
     const int64_t tail_start = head + body4 * 4;
     if (head > 0) {
-        vadd_strided_kernel<<<1, kThreads, 0, stream>>>(a, 1, b, 1, c, 1, head);
+        ST_CUDA_TRY(launch_kernel(vadd_strided_kernel, 1, kThreads, 0, stream, a, 1, b, 1, c, 1, head));
         note_launch();
     }
     if (body4 > 0) {
-        vadd_vec4_kernel<<<grid_for(body4, kThreads * kUnroll, sm_count), kThreads, 0, stream>>>(
-            reinterpret_cast<const float4 *>(a + head), reinterpret_cast<const float4 *>(b + head),
-            reinterpret_cast<float4 *>(c + head), body4);
+        ST_CUDA_TRY(launch_kernel(vadd_vec4_kernel, grid_for(body4, kThreads * kUnroll, sm_count), kThreads, 0, stream,
+                                  reinterpret_cast<const float4 *>(a + head),
+                                  reinterpret_cast<const float4 *>(b + head), reinterpret_cast<float4 *>(c + head),
+                                  body4));
         note_launch();
     }
     if (tail_start < n) {
-        vadd_strided_kernel<<<1, kThreads, 0, stream>>>(a + tail_start, 1, b + tail_start, 1, c + tail_start, 1,
-                                                         n - tail_start);
+        ST_CUDA_TRY(launch_kernel(vadd_strided_kernel, 1, kThreads, 0, stream, a + tail_start, 1, b + tail_start, 1,
+                                  c + tail_start, 1, n - tail_start));
         note_launch();
     }
     const cudaError_t e = cudaPeekAtLastError();
@@ -162,8 +170,8 @@ int launch_vector_add_2d(const float *a, const int64_t sa[2], const float *b, co
                                         stream));
         return ST_OK;
     }
-    vadd_2d_kernel<<<grid_for(rows * cols, kThreads, sm_count), kThreads, 0, stream>>>(
-        a, sa[0], sa[1], b, sb[0], sb[1], c, sc[0], sc[1], rows, cols);
+    ST_CUDA_TRY(launch_kernel(vadd_2d_kernel, grid_for(rows * cols, kThreads, sm_count), kThreads, 0, stream, a, sa[0],
+                              sa[1], b, sb[0], sb[1], c, sc[0], sc[1], rows, cols));
     note_launch();
     const cudaError_t e = cudaPeekAtLastError();
     return e == cudaSuccess ? ST_OK : cuda_fail(cudaGetLastError(), "vadd_2d_kernel");
