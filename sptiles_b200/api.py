@@ -64,8 +64,8 @@ def _exec_for(t: torch.Tensor, flags: int = 0) -> N.StExec:
         # torch's default stream is the legacy NULL stream; NULL would select
         # the context's own stream, so name it explicitly (cudaStreamLegacy)
         ex.stream = handle if handle else CUDA_STREAM_LEGACY
-    else:
-        ex.device = 0
+    else:  # host tensors: the process's current GPU (one rank per GPU), the context's own stream
+        ex.device = torch.cuda.current_device() if torch.cuda.is_available() else 0
         ex.stream = None
     return ex
 
