@@ -590,7 +590,7 @@ def run_reference(args, rank, world):
     wl = WORKLOADS[args.workload]
     threads = os.cpu_count() or 1
     per_step_budget = max(0.3, min(4.0, 150.0 / max(1, args.steps + args.warmup)))
-    vals = []
+    vals, secs = [], []
     if wl["kind"] == "matmul":
         cm = CpuMatmul(wl, threads)
         rows = cm.rows_for(per_step_budget)
@@ -598,6 +598,7 @@ def run_reference(args, rank, world):
             t = cm.run(rows)
             if i >= args.warmup:
                 vals.append(flops_of(wl, rows) / t / 1e12)
+                secs.append(t)
         detail = (f"each step: first {rows} of {wl['m']} rows of C ({rows}x{wl['n']}x{wl['k']}) on {threads} "
                   "threads; CPU restatement of the shader arithmetic (-O3 -ffp-contract=off)")
         unit, cores = "TFLOP/s", threads
@@ -608,14 +609,18 @@ def run_reference(args, rank, world):
             t = cv.run(reps)
             if i >= args.warmup:
                 vals.append(12 * cv.n * reps / t / 1e9)
+                secs.append(t)
         detail = f"each step: {reps} passes over {cv.n} elements, one thread"
         unit, cores = "GB/s", 1
     value = statistics.median(vals)
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": unit, "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "strong",
+        "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(statistics.median(secs) * 1e3, 3),  # one bounded sample (see cpu_baseline)
+        "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": wl.get("dtype", "f32"), "data": "synthetic",
-        "config": config_of(args.workload, wl, args.gpus),
+        "config": {**_config_of(args.workload, wl, args.gpus),
+                   "timed_region": "host wall clock per step, rank 0's host cores"},
         "cpu_baseline": {"value": value, "unit": unit, "cores": cores, "kind": "port", "sample": detail},
         "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "the reference's SPIR-V runs through Vulkan, which is unavailable on this box, and its "
