@@ -154,6 +154,8 @@ struct GemmArgs {
 // Partial accumulators (one 256 x 256 fp32 tile per CTA pair) and arrival
 // flags of the stream-K tail, for up to sm_count / 2 pairs.
 size_t stream_k_workspace_bytes(int sm_count);
+// True when launch_gemm folds split tiles through that workspace (an fp32 C
+// of this GPU alone takes TMA reduce-adds instead and needs none).
 bool gemm_uses_stream_k(const GemmArgs &args, int sm_count);
 size_t stream_k_flag_offset(int sm_count);
 int launch_gemm(const GemmArgs &args, int sm_count, int *dev_err, uint64_t timeout_ns, cudaStream_t stream);

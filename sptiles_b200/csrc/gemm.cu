@@ -90,6 +90,7 @@ struct KParams {
     float *sk_ws;    // stream-K partials (CTA-pair kernel); null: whole tiles only
     int sk_mode;     // stream_k_split mode
     int *sk_flags;   // per (pair, CTA, epilogue warp): partials stored and not yet folded
+    int sk_l2add;    // 1: split units TMA-reduce-add their fp32 partials into C, which holds the bias
     void *c;
     void *c_peers[kMaxPeers];  // the same rows of C in other GPUs' copies (may be empty)
     int n_peers;
@@ -222,7 +223,7 @@ __device__ __forceinline__ void box_get_row(uint32_t box, int lane, uint32_t (&w
 template <int NCOLS>
 __device__ __forceinline__ void store_tile_staged(const KParams &p, const CStoreMaps &cm, uint32_t t_row, int row0,
                                                   int n0, uint32_t staging, int &buf, int lane, int c_begin = 0,
-                                                  int c_end = NCOLS) {
+                                                  int c_end = NCOLS, bool reduce = false) {
     if (row0 >= p.m) return;
     const bool f32 = p.c_dtype == ST_F32;
     const int box_cols = f32 ? 32 : 64;
@@ -234,7 +235,7 @@ __device__ __forceinline__ void store_tile_staged(const KParams &p, const CStore
         if (f32) {
             tmem_load_32(t_row + c0, w);
             tmem_load_wait();
-            if (p.bias != nullptr) add_bias_chunk(p, col0, lane, w);
+            if (p.bias != nullptr && !reduce) add_bias_chunk(p, col0, lane, w);
         } else {
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
@@ -264,12 +265,16 @@ __device__ __forceinline__ void store_tile_staged(const KParams &p, const CStore
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
+            if (reduce) {  // fp32, this GPU's C only
+                tma_reduce_add_2d(&cm.map[0], box, col0, row0);
+            } else {
 #if ST_C_POLICY == 1
-            const uint64_t pol = l2_policy_evict_first();
-            for (int d = 0; d <= p.n_peers; ++d) tma_store_2d_hint(&cm.map[d], box, col0, row0, pol);
+                const uint64_t pol = l2_policy_evict_first();
+                for (int d = 0; d <= p.n_peers; ++d) tma_store_2d_hint(&cm.map[d], box, col0, row0, pol);
 #else
-            for (int d = 0; d <= p.n_peers; ++d) tma_store_2d(&cm.map[d], box, col0, row0);
+                for (int d = 0; d <= p.n_peers; ++d) tma_store_2d(&cm.map[d], box, col0, row0);
 #endif
+            }
             bulk_commit_group();
         }
         buf ^= 1;
@@ -562,7 +567,12 @@ __device__ __forceinline__ uint64_t operand_l2_policy_b() {
 // own (fp32, without waiting), then waits for the others' parts of its own
 // columns, adds them and stores those columns of C.  No unit waits before
 // every unit of its pair has published, and the grid never exceeds the
-// co-resident clusters, so the waits end.  Stream-K index q = P - 1 - pair.
+// co-resident clusters, so the waits end.  Where every tile is split and C is
+// fp32 on this GPU only (sk_l2add), there is no exchange: C is preset to the
+// bias by c_init_f32_kernel and each unit adds its whole partial tile onto C
+// with TMA reduce-adds, which L2 performs (the order of the units' adds, and
+// so the last bit of a sum, can differ between runs).  Stream-K index
+// q = P - 1 - pair.
 enum : int { kUnitWhole = 0, kUnitSplit = 1 };
 
 struct PairWork {
@@ -599,7 +609,8 @@ struct PairSchedule {
     __device__ __forceinline__ void init(const KParams &p, int pair, int num_pairs_, int total) {
         num_pairs = num_pairs_;
         kb = p.num_k_blocks;
-        stream_k_split(total, num_pairs, kb, p.sk_ws != nullptr ? p.sk_mode : 0, dp_tiles, sk_pairs, sk_iters);
+        const bool can_fold = p.sk_ws != nullptr || p.sk_l2add != 0;
+        stream_k_split(total, num_pairs, kb, can_fold ? p.sk_mode : 0, dp_tiles, sk_pairs, sk_iters);
         sk_index = num_pairs - 1 - pair;
     }
     __device__ __forceinline__ long long sk_begin(int q) const {
@@ -1031,14 +1042,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             return tmem_base + (static_cast<uint32_t>(g * 32) << 16) + static_cast<uint32_t>((idx & 1) * kPairN);
         };
         // bias, conversion and the store of accumulator columns [c_begin, c_end)
-        auto store_c = [&](const PairWork &u, int idx, int c_begin, int c_end) {
+        auto store_c = [&](const PairWork &u, int idx, int c_begin, int c_end, bool reduce) {
             int64_t tm, tn;
             tile_raster(num_m_pairs, num_n_pairs, kGroupM, u.tile, tm, tn);
             const int m0 = static_cast<int>(tm) * 2 * kBlockM + static_cast<int>(rank) * kBlockM;
             const int n0 = static_cast<int>(tn) * kPairN;
             const uint32_t t_row = t_row_of(idx);
             if (p.staged) {
-                store_tile_staged<kPairN>(p, cmaps, t_row, m0 + g * 32, n0, staging, sbuf, lane, c_begin, c_end);
+                store_tile_staged<kPairN>(p, cmaps, t_row, m0 + g * 32, n0, staging, sbuf, lane, c_begin, c_end,
+                                          reduce);
             } else {
                 const int row = m0 + g * 32 + lane;
 #pragma unroll 1
@@ -1077,8 +1089,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 ok = false;
                 break;
             }
-            if (w.kind == kUnitWhole) {
-                store_c(w, idx, 0, kPairN);
+            if (w.kind == kUnitWhole || p.sk_l2add) {  // a split unit adds its partial onto C in L2
+                store_c(w, idx, 0, kPairN, w.kind != kUnitWhole);
                 release(idx);
                 continue;
             }
@@ -1113,7 +1125,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             } else {
                 sk_release_reads(p, sched, st, n_split, rank, g, lane);
                 for (int i = 0; i < n_split; ++i) {
-                    store_c(i == 0 ? split_u0 : split_u1, idx - n_split + i, st[i].c_begin, st[i].c_end);
+                    store_c(i == 0 ? split_u0 : split_u1, idx - n_split + i, st[i].c_begin, st[i].c_end, false);
                     release(idx - n_split + i);
                 }
             }
@@ -1642,6 +1654,7 @@ int launch_gemm_3xtf32(const GemmArgs &g, int sm_count, int *dev_err, uint64_t t
     kp.sk_ws = nullptr;
     kp.sk_flags = nullptr;
     kp.sk_mode = 0;
+    kp.sk_l2add = 0;
     kp.staged = 0;  // direct stores
     kp.n_peers = g.peers.n;
     for (int i = 0; i < kMaxPeers; ++i) kp.c_peers[i] = i < g.peers.n ? g.peers.base[i] : nullptr;
@@ -1765,21 +1778,6 @@ int plan_gemm(int in_dtype, int64_t m, int64_t n, int64_t k, int sm_count, GemmP
 // direct stores.  Peer copies always go by TMA store (one asynchronous bulk
 // store per box and destination instead of per-lane stores across NVLink);
 // a local C does unless SPTILES_B200_C_STORE=direct (or =tma) overrides it.
-// Whether launch_gemm would split tiles for these arguments (the stream-K
-// workspace is only acquired then, so other calls put no event between
-// their launches).
-bool gemm_uses_stream_k(const GemmArgs &g, int sm_count) {
-    const int mode = stream_k_mode();
-    if (mode <= 0) return false;
-    GemmPlan plan;
-    if (plan_gemm(g.ab_dtype, g.m, g.n, g.k, sm_count, &plan) != ST_OK || !plan.pair) return false;
-    if (sm_count <= 0) sm_count = 148;
-    int dp = 0, skp = 0;
-    long long ski = 0;
-    stream_k_split(plan.tiles, sm_count / 2, static_cast<int>(cdiv(g.k, plan.block_k)), mode, dp, skp, ski);
-    return skp > 0;
-}
-
 bool c_store_staged(const GemmArgs &g) {
     const int ces = dtype_size(g.c_dtype);
     if ((g.ldc * ces) % 16 != 0) return false;
@@ -1791,6 +1789,71 @@ bool c_store_staged(const GemmArgs &g) {
     if (v != nullptr && std::strcmp(v, "direct") == 0) return false;
     if (v != nullptr && std::strcmp(v, "tma") == 0) return true;
     return ST_C_STORE_DEFAULT != 0;
+}
+
+// How a CTA-pair launch folds the tiles a stream-K schedule splits:
+// kFoldL2Add where every tile is split and C is fp32, staged and on this GPU
+// only (units add their partials onto C preset to the bias);
+// kFoldExchange otherwise (reduce-scatter through the stream-K workspace,
+// whose sums come out the same bit for bit on every run;
+// SPTILES_B200_SK_FOLD=exchange selects it everywhere).
+enum : int { kFoldNone = 0, kFoldExchange = 1, kFoldL2Add = 2 };
+
+int stream_k_fold(const GemmArgs &g, int sm_count) {
+    const int mode = stream_k_mode();
+    if (mode <= 0) return kFoldNone;
+    GemmPlan plan;
+    if (plan_gemm(g.ab_dtype, g.m, g.n, g.k, sm_count, &plan) != ST_OK || !plan.pair) return kFoldNone;
+    if (sm_count <= 0) sm_count = 148;
+    int dp = 0, skp = 0;
+    long long ski = 0;
+    stream_k_split(plan.tiles, sm_count / 2, static_cast<int>(cdiv(g.k, plan.block_k)), mode, dp, skp, ski);
+    if (skp == 0) return kFoldNone;
+    const char *v = std::getenv("SPTILES_B200_SK_FOLD");
+    const bool exchange = v != nullptr && std::strcmp(v, "exchange") == 0;
+    if (!exchange && dp == 0 && g.c_dtype == ST_F32 && g.peers.n == 0 && c_store_staged(g)) return kFoldL2Add;
+    return kFoldExchange;
+}
+
+// Whether launch_gemm folds split tiles through the stream-K workspace (the
+// workspace is only acquired then, so other calls put no event between
+// their launches).
+bool gemm_uses_stream_k(const GemmArgs &g, int sm_count) { return stream_k_fold(g, sm_count) == kFoldExchange; }
+
+// C[r, q] = 0 + bias[q] (0 without a bias) for r < m, q < n: the value the
+// split units of an L2-add stream-K launch add their partial tiles onto.
+// Rows start 16-byte aligned (the staged-C rule), so every full group of
+// four columns goes out as one 16-byte store.
+__global__ void __launch_bounds__(256) c_init_f32_kernel(float *c, long long ldc, const void *bias, int bias_dtype,
+                                                         int m, int n) {
+    pdl_wait();
+    const int n4 = n >> 2;
+    for (int r = blockIdx.x; r < m; r += gridDim.x) {
+        float *row = c + static_cast<long long>(r) * ldc;
+        for (int q = threadIdx.x; q < n4; q += blockDim.x) {
+            float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            if (bias != nullptr) {
+                v.x = 0.0f + load_bias(bias, bias_dtype, 4 * q);
+                v.y = 0.0f + load_bias(bias, bias_dtype, 4 * q + 1);
+                v.z = 0.0f + load_bias(bias, bias_dtype, 4 * q + 2);
+                v.w = 0.0f + load_bias(bias, bias_dtype, 4 * q + 3);
+            }
+            reinterpret_cast<float4 *>(row)[q] = v;
+        }
+        for (int q = 4 * n4 + static_cast<int>(threadIdx.x); q < n; q += blockDim.x)
+            row[q] = bias != nullptr ? 0.0f + load_bias(bias, bias_dtype, q) : 0.0f;
+    }
+    pdl_trigger();
+}
+
+int launch_c_init_f32(const GemmArgs &g, int sm_count, cudaStream_t stream) {
+    const int64_t blocks = g.m < 8LL * sm_count ? g.m : 8LL * sm_count;
+    ST_CUDA_TRY(launch_kernel(c_init_f32_kernel, static_cast<unsigned>(blocks), 256, 0, stream,
+                              static_cast<float *>(g.c), static_cast<long long>(g.ldc), g.bias, g.bias_dtype,
+                              static_cast<int>(g.m), static_cast<int>(g.n)));
+    note_launch();
+    const cudaError_t e = cudaPeekAtLastError();
+    return e == cudaSuccess ? ST_OK : cuda_fail(cudaGetLastError(), "c_init_f32_kernel launch");
 }
 
 int launch_gemm(const GemmArgs &g, int sm_count, int *dev_err, uint64_t timeout_ns, cudaStream_t stream) {
@@ -1836,8 +1899,10 @@ int launch_gemm(const GemmArgs &g, int sm_count, int *dev_err, uint64_t timeout_
     kp.bias_dtype = g.bias_dtype;
     kp.err = dev_err;
     kp.timeout_ns = timeout_ns;
+    const int fold = plan.pair ? stream_k_fold(g, sm_count) : kFoldNone;
     kp.sk_mode = stream_k_mode();
-    kp.sk_ws = plan.pair && kp.sk_mode > 0 ? g.sk_ws : nullptr;
+    kp.sk_l2add = fold == kFoldL2Add ? 1 : 0;
+    kp.sk_ws = fold == kFoldExchange ? g.sk_ws : nullptr;
     kp.sk_flags = kp.sk_ws ? g.sk_flags : nullptr;
     CStoreMaps cm;
     std::memset(&cm, 0, sizeof(cm));
@@ -1854,6 +1919,7 @@ int launch_gemm(const GemmArgs &g, int sm_count, int *dev_err, uint64_t timeout_
     }
     if (plan.pair) {
         const int pairs = plan.ctas / 2;
+        if (kp.sk_l2add) ST_TRY(launch_c_init_f32(g, sm_count > 0 ? sm_count : 148, stream));
         if (g.ab_dtype == ST_F16)
             return g.b_k_major ? launch_pair<0, false>(ma, mb, kp, cm, pairs, stream)
                                : launch_pair<0, true>(ma, mb, kp, cm, pairs, stream);

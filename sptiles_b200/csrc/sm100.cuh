@@ -100,6 +100,16 @@ __device__ __forceinline__ void tma_store_2d_hint(const CUtensorMap *map, uint32
                  : "memory");
 }
 
+// 2D tiled reduction of one shared-memory box into global memory: every
+// element is added (fp32, performed in L2) to the element it lands on.  Same
+// coordinate rules as the store; tracked by the bulk async-groups.
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap *map, uint32_t src, int32_t c0, int32_t c1) {
+    asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(src), "r"(c0), "r"(c1)
+                 : "memory");
+}
+
 __device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 
 // Untiled bulk copies (both addresses 16-byte aligned, size a multiple of 16).

@@ -428,6 +428,65 @@ def test_stream_k_tail_random_bias_16bit_out(monkeypatch, dtype, mnk):
     assert rel_err(C1.cpu().numpy(), C0.cpu().numpy()) <= 1e-5
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16], ids=["f32", "f16", "bf16"])
+@pytest.mark.parametrize("mnk", SK_SHAPES, ids=lambda s: "x".join(map(str, s)))
+def test_stream_k_exchange_fold_known_answers(monkeypatch, dtype, mnk):
+    """fp32 C takes TMA reduce-adds by default; the workspace exchange (the
+    fold of 16-bit C) is forced here for the same shapes."""
+    monkeypatch.setenv("SPTILES_B200_GEMM_KERNEL", "pair")
+    monkeypatch.setenv("SPTILES_B200_SK_FOLD", "exchange")
+    m, n, k = mnk
+    A, B = kat(m, n, k, dtype)
+    C = st.matmul(A, B, out_dtype=torch.float32)
+    assert C.cpu().numpy().tobytes() == oracle.matmul_kat_expected(m, n, k).tobytes()
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16], ids=["f32", "f16"])
+@pytest.mark.parametrize("mnk", [(1024, 1024, 1024), (300, 520, 2000), (1000, 3000, 2000)],
+                         ids=lambda s: "x".join(map(str, s)))
+def test_stream_k_l2add_fold_random_bias(monkeypatch, dtype, mnk):
+    """Split tiles added onto C preset to the bias agree with whole tiles and
+    with the exchange up to summation order, and with the oracle."""
+    monkeypatch.setenv("SPTILES_B200_GEMM_KERNEL", "pair")
+    m, n, k = mnk
+    A, B = normal((m, k), 0.5, 90, dtype), normal((k, n), 0.5, 91, dtype)
+    bias = normal((n,), 1.0, 92, torch.float32)
+    C = st.matmul(A, B, bias, out_dtype=torch.float32)
+    rows = (max(0, m - 256), m)
+    want = oracle_mm(A, B, bias, rows=rows)
+    assert rel_err(C[rows[0]:rows[1]].cpu().numpy(), want) <= (5e-5 if dtype == torch.float32 else TOL[dtype])
+    monkeypatch.setenv("SPTILES_B200_SK_FOLD", "exchange")
+    Cx = st.matmul(A, B, bias, out_dtype=torch.float32)
+    monkeypatch.setenv("SPTILES_B200_STREAM_K", "0")
+    C0 = st.matmul(A, B, bias, out_dtype=torch.float32)
+    # 3xTF32 itself differs from fp32 by ~1e-5, and the split regroups its terms
+    order_tol = 5e-5 if dtype == torch.float32 else 1e-5
+    assert rel_err(C.cpu().numpy(), C0.cpu().numpy()) <= order_tol
+    assert rel_err(Cx.cpu().numpy(), C0.cpu().numpy()) <= order_tol
+
+
+def test_stream_k_l2add_fold_strided_out_and_graph_replay(monkeypatch):
+    """fp32 1024^3: C preset and reduced in place inside a wider buffer (only
+    the [m, n] view changes), captured once and replayed."""
+    monkeypatch.setenv("SPTILES_B200_GEMM_KERNEL", "pair")
+    m, n, k = 1024, 1000, 1024
+    A, B = kat(m, n, k, torch.float32)
+    buf = torch.full((m, n + 24), 7.0, device=DEV)
+    out = buf[:, :n]
+    st.matmul(A, B, out=out)
+    torch.cuda.synchronize()
+    want = oracle.matmul_kat_expected(m, n, k)
+    assert np.array_equal(out.cpu().numpy(), want) and torch.all(buf[:, n:] == 7.0)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        st.matmul(A, B, out=out)
+    for _ in range(3):
+        out.fill_(-1.0)
+        g.replay()
+        torch.cuda.synchronize()
+        assert np.array_equal(out.cpu().numpy(), want) and torch.all(buf[:, n:] == 7.0)
+
+
 def test_stream_k_tail_replays_from_a_cuda_graph(monkeypatch):
     monkeypatch.setenv("SPTILES_B200_GEMM_KERNEL", "pair")
     m, n, k = 1024, 8192, 1024
