@@ -56,6 +56,8 @@ extern "C" {
 /* ---- st_exec.flags ---- */
 #define ST_EXEC_SYNC 1          /* block (bounded by timeout_ms) until the work is done */
 #define ST_EXEC_HOST_BUFFERS 2  /* st_launch only: buffer params are host memory */
+#define ST_EXEC_DETERMINISTIC 4 /* matmul: the same inputs give the same bits on every run (split tiles
+                                   with fp32 C are folded in a fixed order instead of by L2 adds) */
 
 typedef struct st_ctx st_ctx;
 

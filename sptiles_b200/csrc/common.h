@@ -150,6 +150,11 @@ struct GemmArgs {
     // stream_k_workspace_bytes, flags zero when idle
     float *sk_ws = nullptr;
     int *sk_flags = nullptr;
+    // C already holds 0 + bias (the pack kernel preset it): an L2-add
+    // stream-K launch then skips its own preset
+    bool c_preset = false;
+    // fold split tiles in a fixed order (ST_EXEC_DETERMINISTIC)
+    bool deterministic = false;
 };
 // Partial accumulators (one 256 x 256 fp32 tile per CTA pair) and arrival
 // flags of the stream-K tail, for up to sm_count / 2 pairs.
@@ -157,6 +162,9 @@ size_t stream_k_workspace_bytes(int sm_count);
 // True when launch_gemm folds split tiles through that workspace (an fp32 C
 // of this GPU alone takes TMA reduce-adds instead and needs none).
 bool gemm_uses_stream_k(const GemmArgs &args, int sm_count);
+// How launch_gemm folds the tiles a stream-K schedule splits.
+enum : int { kFoldNone = 0, kFoldExchange = 1, kFoldL2Add = 2 };
+int stream_k_fold(const GemmArgs &args, int sm_count);
 size_t stream_k_flag_offset(int sm_count);
 int launch_gemm(const GemmArgs &args, int sm_count, int *dev_err, uint64_t timeout_ns, cudaStream_t stream);
 // fp32 A and B used in place (TMA-addressable): the split into tf32 hi/lo
@@ -174,9 +182,20 @@ int launch_pack_a_tf32(const float *a, int64_t sa0, int64_t sa1, int64_t m, int6
                        cudaStream_t stream);
 int launch_pack_b_tf32(const float *b, int64_t sb0, int64_t sb1, int64_t k, int64_t n, float *bp, int64_t kp,
                        cudaStream_t stream);
-// both in one launch (B's transposing blocks first, then A's rows)
+// C[r, q] = 0 + bias[q] (or 0) for r < m, q < n, fp32, rows 16-byte aligned:
+// the starting value of an L2-add stream-K launch (c == nullptr: nothing)
+struct CPreset {
+    float *c = nullptr;
+    long long ldc = 0;
+    const void *bias = nullptr;
+    int bias_dtype = ST_F32;
+    int m = 0, n = 0;
+};
+// both in one launch (B's transposing blocks first, then A's rows, whose
+// blocks also write `preset`'s C when given)
 int launch_pack_ab_tf32(const float *a, int64_t sa0, int64_t sa1, int64_t m, const float *b, int64_t sb0,
-                        int64_t sb1, int64_t n, int64_t k, float *ap, float *bp, int64_t kp, cudaStream_t stream);
+                        int64_t sb1, int64_t n, int64_t k, float *ap, float *bp, int64_t kp,
+                        const CPreset *preset, cudaStream_t stream);
 // Copy a 16-bit [rows, cols] matrix with arbitrary element strides into a
 // dense row-major [rows, ld] buffer (ld >= cols, padding columns zeroed).
 int launch_repack_16(const uint16_t *src, int64_t s0, int64_t s1, int64_t rows, int64_t cols, uint16_t *dst,

@@ -1795,10 +1795,9 @@ bool c_store_staged(const GemmArgs &g) {
 // kFoldL2Add where every tile is split and C is fp32, staged and on this GPU
 // only (units add their partials onto C preset to the bias);
 // kFoldExchange otherwise (reduce-scatter through the stream-K workspace,
-// whose sums come out the same bit for bit on every run;
-// SPTILES_B200_SK_FOLD=exchange selects it everywhere).
-enum : int { kFoldNone = 0, kFoldExchange = 1, kFoldL2Add = 2 };
-
+// whose sums come out the same bit for bit on every run; callers that ask
+// for that pass ST_EXEC_DETERMINISTIC, and SPTILES_B200_SK_FOLD=exchange
+// selects it everywhere).
 int stream_k_fold(const GemmArgs &g, int sm_count) {
     const int mode = stream_k_mode();
     if (mode <= 0) return kFoldNone;
@@ -1811,7 +1810,8 @@ int stream_k_fold(const GemmArgs &g, int sm_count) {
     if (skp == 0) return kFoldNone;
     const char *v = std::getenv("SPTILES_B200_SK_FOLD");
     const bool exchange = v != nullptr && std::strcmp(v, "exchange") == 0;
-    if (!exchange && dp == 0 && g.c_dtype == ST_F32 && g.peers.n == 0 && c_store_staged(g)) return kFoldL2Add;
+    if (!exchange && !g.deterministic && dp == 0 && g.c_dtype == ST_F32 && g.peers.n == 0 && c_store_staged(g))
+        return kFoldL2Add;
     return kFoldExchange;
 }
 
@@ -1919,7 +1919,7 @@ int launch_gemm(const GemmArgs &g, int sm_count, int *dev_err, uint64_t timeout_
     }
     if (plan.pair) {
         const int pairs = plan.ctas / 2;
-        if (kp.sk_l2add) ST_TRY(launch_c_init_f32(g, sm_count > 0 ? sm_count : 148, stream));
+        if (kp.sk_l2add && !g.c_preset) ST_TRY(launch_c_init_f32(g, sm_count > 0 ? sm_count : 148, stream));
         if (g.ab_dtype == ST_F16)
             return g.b_k_major ? launch_pair<0, false>(ma, mb, kp, cm, pairs, stream)
                                : launch_pair<0, true>(ma, mb, kp, cm, pairs, stream);

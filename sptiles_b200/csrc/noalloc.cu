@@ -199,6 +199,7 @@ extern "C" int st_matmul_static_scratch(const st_tensor *a, const st_tensor *b, 
         g.m = M;
         g.n = N;
         g.k = 3 * kp;
+        g.deterministic = exec != nullptr && (exec->flags & ST_EXEC_DETERMINISTIC) != 0;
         ST_TRY(launch_gemm(g, sd->sm_count, sd->abort_word, kWaitLimitNs, stream));
     }
     if (exec && (exec->flags & ST_EXEC_SYNC)) {

@@ -17,6 +17,8 @@
 //
 // 16-bit inputs whose strides TMA cannot address are copied into a dense
 // row-major scratch matrix first (repack_16).
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -94,13 +96,24 @@ __global__ void __launch_bounds__(kThreads) pack_b_kernel(const float *__restric
     pdl_trigger();
 }
 
+__device__ __forceinline__ float preset_bias(const CPreset &p, int q) {
+    if (p.bias == nullptr) return 0.0f;
+    float v;
+    if (p.bias_dtype == ST_F32) v = static_cast<const float *>(p.bias)[q];
+    else if (p.bias_dtype == ST_F16) v = __half2float(static_cast<const __half *>(p.bias)[q]);
+    else v = __bfloat162float(static_cast<const __nv_bfloat16 *>(p.bias)[q]);
+    return 0.0f + v;  // -0 becomes +0, as an accumulator that starts at +0 would give
+}
+
 // Both operands in one launch: blocks [0, tiles_b) transpose B's 32 x 32
-// tiles (as pack_b_kernel), the rest split A's rows (as pack_a_kernel).
+// tiles (as pack_b_kernel), the rest split A's rows (as pack_a_kernel) and
+// then, when preset.c is set, write C's starting value (one 16-byte store
+// per four columns; rows are 16-byte aligned).
 __global__ void __launch_bounds__(kThreads) pack_ab_kernel(const float *__restrict__ a, int64_t sa0, int64_t sa1,
                                                            int64_t m, const float *__restrict__ b, int64_t sb0,
                                                            int64_t sb1, int64_t n, int64_t k, int64_t kp,
                                                            float *__restrict__ ap, float *__restrict__ bp,
-                                                           int tiles_k, int tiles_b) {
+                                                           int tiles_k, int tiles_b, const CPreset preset) {
     pdl_wait();
     __shared__ float hi_t[32][33];
     __shared__ float lo_t[32][33];
@@ -146,6 +159,22 @@ __global__ void __launch_bounds__(kThreads) pack_ab_kernel(const float *__restri
         row[k0 / 4] = h;
         row[(kp + k0) / 4] = h;
         row[(2 * kp + k0) / 4] = make_float4(lo[0], lo[1], lo[2], lo[3]);
+    }
+    if (preset.c != nullptr) {
+        const int quads = (preset.n + 3) / 4;
+        const int64_t cells = static_cast<int64_t>(preset.m) * quads;
+        for (int64_t i = static_cast<int64_t>(blockIdx.x - tiles_b) * kThreads + threadIdx.x; i < cells; i += step) {
+            const int r = static_cast<int>(i / quads);
+            const int q0 = static_cast<int>(i - static_cast<int64_t>(r) * quads) * 4;
+            float *row = preset.c + static_cast<int64_t>(r) * preset.ldc;
+            if (q0 + 4 <= preset.n) {
+                reinterpret_cast<float4 *>(row)[q0 / 4] = make_float4(
+                    preset_bias(preset, q0), preset_bias(preset, q0 + 1), preset_bias(preset, q0 + 2),
+                    preset_bias(preset, q0 + 3));
+            } else {
+                for (int q = q0; q < preset.n; ++q) row[q] = preset_bias(preset, q);
+            }
+        }
     }
     pdl_trigger();
 }
@@ -193,16 +222,21 @@ int launch_pack_b_tf32(const float *b, int64_t sb0, int64_t sb1, int64_t k, int6
 }
 
 int launch_pack_ab_tf32(const float *a, int64_t sa0, int64_t sa1, int64_t m, const float *b, int64_t sb0,
-                        int64_t sb1, int64_t n, int64_t k, float *ap, float *bp, int64_t kp, cudaStream_t stream) {
+                        int64_t sb1, int64_t n, int64_t k, float *ap, float *bp, int64_t kp, const CPreset *preset,
+                        cudaStream_t stream) {
     if (kp <= 0 || (m <= 0 && n <= 0)) return ST_OK;
+    const CPreset cp = preset != nullptr && preset->m > 0 && preset->n > 0 ? *preset : CPreset{};
+    if (cp.c != nullptr && (reinterpret_cast<uintptr_t>(cp.c) % 16 != 0 || cp.ldc % 4 != 0))
+        return fail(ST_ERR_INVALID_ARGUMENT, "C preset needs 16-byte aligned rows");
     const int64_t tiles_k = cdiv(kp, 32);
     const int64_t tiles_b = n > 0 ? tiles_k * cdiv(n, 32) : 0;
-    const int64_t blocks_a = m > 0 ? grid_1d(m * (kp / 4)) : 0;
+    int64_t blocks_a = m > 0 ? grid_1d(m * (kp / 4)) : 0;
+    if (cp.c != nullptr && blocks_a == 0) blocks_a = grid_1d(static_cast<int64_t>(cp.m) * ((cp.n + 3) / 4));
     if (tiles_b + blocks_a > (int64_t(1) << 31) - 1)
         return fail(ST_ERR_UNSUPPORTED, "fp32 operands too large for one pack launch");
     ST_CUDA_TRY(launch_kernel(pack_ab_kernel, static_cast<unsigned>(tiles_b + blocks_a), kThreads, 0, stream, a, sa0,
-                              sa1, blocks_a > 0 ? m : 0, b, sb0, sb1, n, k, kp, ap, bp, static_cast<int>(tiles_k),
-                              static_cast<int>(tiles_b)));
+                              sa1, m > 0 ? m : 0, b, sb0, sb1, n, k, kp, ap, bp, static_cast<int>(tiles_k),
+                              static_cast<int>(tiles_b), cp));
     note_launch();
     const cudaError_t e = cudaPeekAtLastError();
     return e == cudaSuccess ? ST_OK : cuda_fail(cudaGetLastError(), "pack_ab_kernel");

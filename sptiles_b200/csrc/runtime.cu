@@ -362,6 +362,7 @@ int matmul_device(const ExecCtx &x, const st_tensor &a, const st_tensor &b, cons
     }
     GemmArgs g{};
     if (peers) g.peers = *peers;
+    g.deterministic = (x.flags & ST_EXEC_DETERMINISTIC) != 0;
     g.c = c.data;
     g.ldc = c.strides[0];
     g.c_dtype = c.dtype;
@@ -396,9 +397,6 @@ int matmul_device(const ExecCtx &x, const st_tensor &a, const st_tensor &b, cons
         ST_TRY(ws_acquire(ws, need, x.stream, &base));
         float *ap = static_cast<float *>(base);
         float *bp = ap + M * 3 * kp;
-        ST_TRY(launch_pack_ab_tf32(static_cast<const float *>(a.data), a.strides[0], a.strides[1], M,
-                                   static_cast<const float *>(b.data), b.strides[0], b.strides[1], N, K, ap, bp, kp,
-                                   x.stream));
         g.ab_dtype = ST_F32;
         g.a = ap;
         g.lda = 3 * kp;
@@ -406,6 +404,20 @@ int matmul_device(const ExecCtx &x, const st_tensor &a, const st_tensor &b, cons
         g.ldb = 3 * kp;
         g.b_k_major = true;
         g.k = 3 * kp;
+        // an L2-add stream-K launch starts from C = bias: the pack writes it
+        CPreset preset;
+        if (stream_k_fold(g, x.dev->sm_count) == kFoldL2Add) {
+            preset.c = static_cast<float *>(c.data);
+            preset.ldc = c.strides[0];
+            preset.bias = bias_ptr;
+            preset.bias_dtype = bias_dtype;
+            preset.m = static_cast<int>(M);
+            preset.n = static_cast<int>(N);
+            g.c_preset = true;
+        }
+        ST_TRY(launch_pack_ab_tf32(static_cast<const float *>(a.data), a.strides[0], a.strides[1], M,
+                                   static_cast<const float *>(b.data), b.strides[0], b.strides[1], N, K, ap, bp, kp,
+                                   g.c_preset ? &preset : nullptr, x.stream));
         if (gemm_uses_stream_k(g, x.dev->sm_count)) ST_TRY(sk_acquire(x.dev, x.stream, g));
         ST_TRY(launch_gemm(g, x.dev->sm_count, x.dev->dev_err, kDeviceWaitLimitNs, x.stream));
         if (g.sk_ws) ST_TRY(ws_release(x.dev->sk, x.stream));

@@ -8,6 +8,7 @@ The reference's known-answer inputs make every partial sum exact, so those
 cases are compared bit for bit, at the benchmark configurations' full sizes
 as well.
 """
+import contextlib
 import ctypes
 import json
 from pathlib import Path
@@ -49,6 +50,18 @@ def oracle_mm(A, B, bias=None, rows=None, out=oracle.F32):
     bf = A.dtype == torch.bfloat16
     return oracle.matmul(to_np(A), to_np(B), None if bias is None else to_np(bias), bf16=bf, out_dtype=out,
                          rows=rows)
+
+
+@contextlib.contextmanager
+def deterministic():
+    """torch.use_deterministic_algorithms(True) for the block (the library then
+    passes ST_EXEC_DETERMINISTIC)."""
+    prev = torch.are_deterministic_algorithms_enabled()
+    torch.use_deterministic_algorithms(True)
+    try:
+        yield
+    finally:
+        torch.use_deterministic_algorithms(prev)
 
 
 def kat(m, n, k, dtype):
@@ -307,9 +320,11 @@ def test_host_tensors_chunked_pipeline(pinned, dtype):
     for r0, r1 in ((0, 8), (1784, 1800), (m - 8, m)):  # both chunks and the seam
         want = oracle_mm(A, B, bias, rows=(r0, r1))
         assert rel_err(C[r0:r1].numpy(), want) <= TOL[dtype]
-    # padded host output rows
-    out = torch.full((m, n + 3), 7.0)
-    st.matmul(A, B, bias, out=out[:, :n])
+    # padded host output rows; the same bits as a first call in deterministic mode
+    with deterministic():
+        C = st.matmul(A, B, bias, out_dtype=torch.float32)
+        out = torch.full((m, n + 3), 7.0)
+        st.matmul(A, B, bias, out=out[:, :n])
     assert torch.equal(out[:, :n], C) and torch.all(out[:, n:] == 7.0)
 
 
@@ -463,6 +478,26 @@ def test_stream_k_l2add_fold_random_bias(monkeypatch, dtype, mnk):
     order_tol = 5e-5 if dtype == torch.float32 else 1e-5
     assert rel_err(C.cpu().numpy(), C0.cpu().numpy()) <= order_tol
     assert rel_err(Cx.cpu().numpy(), C0.cpu().numpy()) <= order_tol
+
+
+@pytest.mark.parametrize("mnk", [(1024, 1024, 1024), (300, 520, 2000)], ids=lambda s: "x".join(map(str, s)))
+def test_deterministic_mode_repeats_bit_for_bit(monkeypatch, mnk):
+    """Split tiles with fp32 C: L2 adds by default (last-bit differences
+    between runs allowed), a fixed-order fold under deterministic mode."""
+    monkeypatch.setenv("SPTILES_B200_GEMM_KERNEL", "pair")
+    m, n, k = mnk
+    A, B = normal((m, k), 1.0, 95, torch.float32), normal((k, n), 1.0, 96, torch.float32)
+    bias = normal((n,), 1.0, 97, torch.float32)
+    runs = [st.matmul(A, B, bias) for _ in range(3)]
+    for r in runs[1:]:
+        assert rel_err(r.cpu().numpy(), runs[0].cpu().numpy()) <= 1e-6
+    with deterministic():
+        det = [st.matmul(A, B, bias) for _ in range(4)]
+        host = st.matmul(A.cpu(), B.cpu(), bias.cpu())
+    for r in det[1:]:
+        assert torch.equal(r, det[0])
+    assert rel_err(host.numpy(), det[0].cpu().numpy()) <= 1e-6
+    assert rel_err(det[0].cpu().numpy(), runs[0].cpu().numpy()) <= 5e-5
 
 
 def test_stream_k_l2add_fold_strided_out_and_graph_replay(monkeypatch):
