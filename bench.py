@@ -182,6 +182,17 @@ def make_matmul_inputs(wl, rows, device, seed_offset=0):
     return a, b, bias
 
 
+def matmul_buffer_sets(wl, rows):
+    """Buffer sets a matmul step rotates through: operands and C that fit in
+    the L2 (fp32 1024^3: 12 MB) get enough copies that one pass over them
+    exceeds twice the L2, so every step reads its inputs from HBM."""
+    elem = {"f32": 4, "f16": 2, "bf16": 2}
+    set_bytes = (rows * wl["k"] + wl["k"] * wl["n"]) * elem[wl["dtype"]] + rows * wl["n"] * elem[wl["out"]]
+    if rows == 0 or set_bytes > L2_BYTES:
+        return 1
+    return min(64, math.ceil(2 * L2_BYTES / set_bytes))
+
+
 def flops_of(wl, rows):
     f = 2.0 * rows * wl["n"] * wl["k"]
     if wl["bias"]:
@@ -288,13 +299,16 @@ def run_matmul(wl, args, rank, world, local, dist_on, peaks):
     if replicate == "fused":
         from sptiles_b200.partition import ReplicatedOutput
         rep = ReplicatedOutput(wl["m"], wl["n"], out_dt)
+    sets = 1 if replicate else matmul_buffer_sets(wl, rows)
+    bufs = [(a, b, c)] + [(a.clone(), b.clone(), torch.empty_like(c)) for _ in range(sets - 1)]
 
-    def step(_i):
+    def step(i):
         if rep is not None:
             rep.matmul(a, b, bias)
             return
         if rows:
-            st.matmul(a, b, bias, out=c)
+            aa, bb, cc = bufs[i % sets]
+            st.matmul(aa, bb, bias, out=cc)
         if replicate:
             gather_rows()
 
@@ -363,6 +377,7 @@ def run_matmul(wl, args, rank, world, local, dist_on, peaks):
                clocks=clk.summary(), plan=plan, rows=rows, allgather=gather)
     if rep is not None:
         rep.close()
+    del bufs[1:]
     if not args.no_e2e:
         out["e2e"] = e2e_matmul(wl, args, a, b, bias, out_dt, rows, dist_on)
     return out
@@ -638,12 +653,18 @@ def config_of(name, wl, n_gpus, timing="auto"):
     return cfg
 
 
+def _matmul_l2_note(wl, n_gpus):
+    sets = matmul_buffer_sets(wl, -(-wl["m"] // n_gpus))
+    if sets == 1:
+        return "inputs exceed L2 (A + B + C per rank > 126 MB)"
+    return f"steps rotate through {sets} buffer sets of A, B, C totalling > 2x L2"
+
+
 def _config_of(name, wl, n_gpus):
     if wl["kind"] == "matmul":
         return {"workload": name, "M": wl["m"], "N": wl["n"], "K": wl["k"], "in_dtype": wl["dtype"],
                 "out_dtype": wl["out"], "bias": wl["bias"], "parallelism": f"M-row shards x{n_gpus}",
-                "l2": "inputs exceed L2 (A+B > 126 MB)" if wl["m"] * wl["k"] * 2 > L2_BYTES else
-                      "inputs fit in L2"}
+                "l2": _matmul_l2_note(wl, n_gpus)}
     total = math.prod(wl["shape"])
     return {"workload": name, "shape": list(wl["shape"]), "dtype": "f32", "parallelism": f"element shards x{n_gpus}",
             "l2": "steps rotate through buffer sets totalling > 2x L2"}

@@ -121,58 +121,99 @@ __global__ void __launch_bounds__(kThreads) pack_ab_kernel(const float *__restri
         const int64_t k0 = static_cast<int64_t>(blockIdx.x % tiles_k) * 32;
         const int64_t n0 = static_cast<int64_t>(blockIdx.x / tiles_k) * 32;
         const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8
-        for (int r = ty; r < 32; r += 8) {
-            const int64_t kk = k0 + r, nn = n0 + tx;
-            const float x = (kk < k && nn < n) ? b[kk * sb0 + nn * sb1] : 0.0f;
-            const float h = tf32_round(x);
-            hi_t[r][tx] = h;
-            lo_t[r][tx] = tf32_round(x - h);
+        // 16-byte path: thread (r, c) = (tid / 8, tid % 8) loads B[k0 + r][n0 + 4c ..
+        // + 3]; the [k][n] tiles (row pitch 33) stay free of bank conflicts
+        const int vr = threadIdx.x >> 3, vc = threadIdx.x & 7;
+        const bool full_n = n0 + 32 <= n;
+        if (full_n && k0 + 32 <= k && sb1 == 1 && sb0 % 4 == 0 && reinterpret_cast<uintptr_t>(b) % 16 == 0) {
+            const float4 v = *reinterpret_cast<const float4 *>(b + (k0 + vr) * sb0 + n0 + 4 * vc);
+            const float x[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+                const float h = tf32_round(x[t]);
+                hi_t[vr][4 * vc + t] = h;
+                lo_t[vr][4 * vc + t] = tf32_round(x[t] - h);
+            }
+        } else {
+            for (int r = ty; r < 32; r += 8) {
+                const int64_t kk = k0 + r, nn = n0 + tx;
+                const float x = (kk < k && nn < n) ? b[kk * sb0 + nn * sb1] : 0.0f;
+                const float h = tf32_round(x);
+                hi_t[r][tx] = h;
+                lo_t[r][tx] = tf32_round(x - h);
+            }
         }
         __syncthreads();
-        for (int r = ty; r < 32; r += 8) {
-            const int64_t nn = n0 + r, kk = k0 + tx;
-            if (nn < n && kk < kp) {
-                float *row = bp + nn * 3 * kp;
-                const float h = hi_t[tx][r];
-                row[kk] = h;
-                row[kp + kk] = lo_t[tx][r];
-                row[2 * kp + kk] = h;
+        if (full_n) {  // row n0 + vr of Bp, K elements k0 + 4c .. + 3 of each segment (k0 + 32 <= kp)
+            const int kq = 4 * vc;
+            const float4 h = make_float4(hi_t[kq][vr], hi_t[kq + 1][vr], hi_t[kq + 2][vr], hi_t[kq + 3][vr]);
+            const float4 l = make_float4(lo_t[kq][vr], lo_t[kq + 1][vr], lo_t[kq + 2][vr], lo_t[kq + 3][vr]);
+            float *row = bp + (n0 + vr) * 3 * kp + k0 + kq;
+            *reinterpret_cast<float4 *>(row) = h;
+            *reinterpret_cast<float4 *>(row + kp) = l;
+            *reinterpret_cast<float4 *>(row + 2 * kp) = h;
+        } else {
+            for (int r = ty; r < 32; r += 8) {
+                const int64_t nn = n0 + r, kk = k0 + tx;
+                if (nn < n && kk < kp) {
+                    float *row = bp + nn * 3 * kp;
+                    const float h = hi_t[tx][r];
+                    row[kk] = h;
+                    row[kp + kk] = lo_t[tx][r];
+                    row[2 * kp + kk] = h;
+                }
             }
         }
         return;
     }
-    const int64_t groups = kp / 4;
-    const int64_t total = m * groups;
-    const int64_t step = static_cast<int64_t>(gridDim.x - tiles_b) * kThreads;
-    for (int64_t i = static_cast<int64_t>(blockIdx.x - tiles_b) * kThreads + threadIdx.x; i < total; i += step) {
-        const int64_t r = i / groups;
-        const int64_t k0 = (i - r * groups) * 4;
-        float hi[4], lo[4];
+    // A's rows, then C's preset rows: block j of the rest handles rows j,
+    // j + blocks, ... (no index division), one 4-element group per thread
+    // and pass; 16-byte loads when A's rows are dense and aligned
+    const int64_t blocks = static_cast<int64_t>(gridDim.x) - tiles_b;
+    const int64_t j0 = static_cast<int64_t>(blockIdx.x) - tiles_b;
+    const int groups = static_cast<int>(kp / 4);
+    const bool a_vec = sa1 == 1 && sa0 % 4 == 0 && reinterpret_cast<uintptr_t>(a) % 16 == 0;
+    for (int64_t r = j0; r < m; r += blocks) {
+        const float *arow = a + r * sa0;
+        float4 *prow = reinterpret_cast<float4 *>(ap + r * 3 * kp);
+        for (int q = threadIdx.x; q < groups; q += kThreads) {
+            const int64_t k0 = 4 * static_cast<int64_t>(q);
+            float x[4];
+            if (a_vec && k0 + 4 <= k) {
+                const float4 v = *reinterpret_cast<const float4 *>(arow + k0);
+                x[0] = v.x;
+                x[1] = v.y;
+                x[2] = v.z;
+                x[3] = v.w;
+            } else {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const float x = (k0 + j < k) ? a[r * sa0 + (k0 + j) * sa1] : 0.0f;
-            hi[j] = tf32_round(x);
-            lo[j] = tf32_round(x - hi[j]);
+                for (int t = 0; t < 4; ++t) x[t] = k0 + t < k ? arow[(k0 + t) * sa1] : 0.0f;
+            }
+            float hi[4], lo[4];
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+                hi[t] = tf32_round(x[t]);
+                lo[t] = tf32_round(x[t] - hi[t]);
+            }
+            const float4 h = make_float4(hi[0], hi[1], hi[2], hi[3]);
+            prow[q] = h;
+            prow[groups + q] = h;
+            prow[2 * groups + q] = make_float4(lo[0], lo[1], lo[2], lo[3]);
         }
-        float4 *row = reinterpret_cast<float4 *>(ap + r * 3 * kp);
-        const float4 h = make_float4(hi[0], hi[1], hi[2], hi[3]);
-        row[k0 / 4] = h;
-        row[(kp + k0) / 4] = h;
-        row[(2 * kp + k0) / 4] = make_float4(lo[0], lo[1], lo[2], lo[3]);
     }
     if (preset.c != nullptr) {
         const int quads = (preset.n + 3) / 4;
-        const int64_t cells = static_cast<int64_t>(preset.m) * quads;
-        for (int64_t i = static_cast<int64_t>(blockIdx.x - tiles_b) * kThreads + threadIdx.x; i < cells; i += step) {
-            const int r = static_cast<int>(i / quads);
-            const int q0 = static_cast<int>(i - static_cast<int64_t>(r) * quads) * 4;
-            float *row = preset.c + static_cast<int64_t>(r) * preset.ldc;
-            if (q0 + 4 <= preset.n) {
-                reinterpret_cast<float4 *>(row)[q0 / 4] = make_float4(
-                    preset_bias(preset, q0), preset_bias(preset, q0 + 1), preset_bias(preset, q0 + 2),
-                    preset_bias(preset, q0 + 3));
-            } else {
-                for (int q = q0; q < preset.n; ++q) row[q] = preset_bias(preset, q);
+        for (int64_t r = j0; r < preset.m; r += blocks) {
+            float *row = preset.c + r * preset.ldc;
+            for (int q = threadIdx.x; q < quads; q += kThreads) {
+                const int q0 = 4 * q;
+                if (q0 + 4 <= preset.n) {
+                    reinterpret_cast<float4 *>(row)[q] =
+                        make_float4(preset_bias(preset, q0), preset_bias(preset, q0 + 1),
+                                    preset_bias(preset, q0 + 2), preset_bias(preset, q0 + 3));
+                } else {
+                    for (int c = q0; c < preset.n; ++c) row[c] = preset_bias(preset, c);
+                }
             }
         }
     }
@@ -230,8 +271,10 @@ int launch_pack_ab_tf32(const float *a, int64_t sa0, int64_t sa1, int64_t m, con
         return fail(ST_ERR_INVALID_ARGUMENT, "C preset needs 16-byte aligned rows");
     const int64_t tiles_k = cdiv(kp, 32);
     const int64_t tiles_b = n > 0 ? tiles_k * cdiv(n, 32) : 0;
-    int64_t blocks_a = m > 0 ? grid_1d(m * (kp / 4)) : 0;
-    if (cp.c != nullptr && blocks_a == 0) blocks_a = grid_1d(static_cast<int64_t>(cp.m) * ((cp.n + 3) / 4));
+    // one block per row of A (or of C's preset), at most 148 x 16
+    const int64_t rows = m > cp.m ? m : cp.m;
+    const int64_t blocks_a = rows > 0 ? (rows < 148 * 16 ? rows : 148 * 16) : 0;
+    if (kp / 4 > (int64_t(1) << 30)) return fail(ST_ERR_UNSUPPORTED, "fp32 K too large for one pack launch");
     if (tiles_b + blocks_a > (int64_t(1) << 31) - 1)
         return fail(ST_ERR_UNSUPPORTED, "fp32 operands too large for one pack launch");
     ST_CUDA_TRY(launch_kernel(pack_ab_kernel, static_cast<unsigned>(tiles_b + blocks_a), kThreads, 0, stream, a, sa0,
