@@ -154,6 +154,54 @@ int st_launch(st_ctx *ctx, const char *entry_name, const st_grid *grid,
 int st_grid_from_dispatch(const char *entry_name, const uint32_t dispatch[3], int64_t tile_elems,
                           st_grid *out);
 
+/* ---- cuda_tile modules (TileIR bytecode, .tilebc): entry discovery.
+ * Replace the translator's module loading (src/main.cpp:75-104:
+ * load_cuda_tile_file, isTileIRBytecode, readBytecode) and its derivation of
+ * the launch ABI from each cuda_tile.entry (src/lower.hpp:197-310:
+ * replace_entries, convert_entry_type, attach_spirv_abi_attrs -- parameter i
+ * is binding i; tile<ptr<T>> is a buffer, tile<i32> an i32 scalar).  Only the
+ * entries' symbols and parameter types, their sm_100 hints and the tile
+ * shapes of the module's partition views are read; function bodies are
+ * skipped, never decoded or run.  Bytecode versions 13.1 to 13.3. */
+typedef struct st_module st_module;
+
+#define ST_MODULE_PARAM_BUFFER 0 /* tile<ptr<T>>: the data of an array */
+#define ST_MODULE_PARAM_I32 1    /* tile<i32>: a size or stride */
+#define ST_MODULE_PARAM_OTHER 2  /* any other parameter type (not launchable here) */
+
+typedef struct {
+    const char *name;           /* entry symbol (valid until st_module_free) */
+    int32_t n_params;           /* parameters = bindings, in order */
+    int32_t n_arrays;           /* cutile_python_v1 array descriptors they form (0: none) */
+    int32_t array_rank[8];
+    int32_t array_dtype[8];     /* ST_F32 / ST_F16 / ST_BF16, -1 for other element types */
+    int32_t n_constants;        /* tile sizes recovered from the module; 0 = not unambiguous */
+    int32_t constants[3];       /* vector_add: tile_size (1D) or tile_m, tile_n; matmul: tm, tn, tk */
+    int32_t num_cta_in_cga;     /* sm_100 entry hint, 0 when absent */
+    int32_t occupancy;          /* sm_100 entry hint, 0 when absent */
+    const char *backend_entry;  /* st_launch registry entry serving it; NULL = none */
+} st_module_entry_info;
+
+/* Parse a module held in memory (the bytes are not kept). */
+int st_module_load(const void *bytes, uint64_t size, st_module **out);
+/* Read and parse a .tilebc file (load_cuda_tile_file, main.cpp:87-104; MLIR
+ * text input is not accepted). */
+int st_module_load_file(const char *path, st_module **out);
+int st_module_free(st_module *module);
+int st_module_version(const st_module *module, int32_t *major, int32_t *minor, int32_t *tag);
+int st_module_entry_count(const st_module *module, int32_t *count);
+int st_module_entry(const st_module *module, int32_t index, st_module_entry_info *out);
+/* Kind (ST_MODULE_PARAM_*) and element type of one entry parameter. */
+int st_module_param(const st_module *module, int32_t entry, int32_t param, int32_t *kind, int32_t *dtype);
+/* st_launch of a module entry (run_compute with the module's entry name,
+ * examples.cpp:271-448).  entry_name may be NULL for a one-entry module.
+ * The bindings must match the entry's parameters in kind and element type;
+ * the module's tile sizes are appended unless the caller passes its own as
+ * trailing i32 constants (required when n_constants is 0).  The grid counts
+ * tile blocks, as for st_launch. */
+int st_launch_module(st_ctx *ctx, const st_module *module, const char *entry_name, const st_grid *grid,
+                     const st_param *params, int32_t n_params, const st_exec *exec);
+
 /* ---- typed calls (device memory) ---- */
 /* C = A + B elementwise over the whole of C (rank 1 or 2, f32, any strides). */
 int st_vector_add(st_ctx *ctx, const st_tensor *a, const st_tensor *b, const st_tensor *c,

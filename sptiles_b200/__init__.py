@@ -16,6 +16,7 @@ from .runtime import (  # noqa: F401
     run_tile_kernel,
     shard_range, shutdown, stream_k_split, sync, tensor_1d_descriptor, tensor_2d_descriptor, tile_raster,
 )
+from .module import ModuleEntry, TileModule  # noqa: F401
 from ._native import DeviceAbort, NativeError, lib  # noqa: F401
 
 __version__ = "0.1.0"

@@ -26,6 +26,7 @@ ST_ERR_DEVICE_ABORT = 8
 
 ST_F32, ST_F16, ST_BF16, ST_I32 = 0, 1, 2, 3
 ST_PARAM_BUFFER, ST_PARAM_I32 = 0, 1
+ST_MODULE_PARAM_BUFFER, ST_MODULE_PARAM_I32, ST_MODULE_PARAM_OTHER = 0, 1, 2
 ST_EXEC_SYNC, ST_EXEC_HOST_BUFFERS, ST_EXEC_DETERMINISTIC = 1, 2, 4
 
 # Every symbol the header declares; the CPU test suite checks the library exports them all.
@@ -35,6 +36,8 @@ EXPORTED = (
     "st_vector_add", "st_matmul", "st_vector_add_host", "st_matmul_host", "st_tile_raster",
     "st_matmul_plan", "st_stream_k_split", "st_shard_range", "st_matmul_static_scratch", "st_vector_fma", "st_cast",
     "st_ipc_handle", "st_ipc_open", "st_ipc_close", "st_matmul_allgather",
+    "st_module_load", "st_module_load_file", "st_module_free", "st_module_version", "st_module_entry_count",
+    "st_module_entry", "st_module_param", "st_launch_module",
 )
 
 
@@ -56,6 +59,14 @@ class StExec(ctypes.Structure):
     _fields_ = [("stream", ctypes.c_void_p), ("device", ctypes.c_int32), ("flags", ctypes.c_int32),
                 ("timeout_ms", ctypes.c_uint32), ("output_indices", ctypes.POINTER(ctypes.c_int32)),
                 ("n_outputs", ctypes.c_int32)]
+
+
+class StModuleEntryInfo(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char_p), ("n_params", ctypes.c_int32), ("n_arrays", ctypes.c_int32),
+                ("array_rank", ctypes.c_int32 * 8), ("array_dtype", ctypes.c_int32 * 8),
+                ("n_constants", ctypes.c_int32), ("constants", ctypes.c_int32 * 3),
+                ("num_cta_in_cga", ctypes.c_int32), ("occupancy", ctypes.c_int32),
+                ("backend_entry", ctypes.c_char_p)]
 
 
 class NativeError(RuntimeError):
@@ -111,6 +122,14 @@ def _declare(L: ctypes.CDLL) -> None:
         "st_shard_range": ([i64, i32, i32, i64, _P(i64), _P(i64)], _c.c_int),
         "st_matmul_static_scratch": ([_P(StTensor), _P(StTensor), _P(StTensor), _P(StTensor), _P(StExec)],
                                      _c.c_int),
+        "st_module_load": ([vp, u64, _P(vp)], _c.c_int),
+        "st_module_load_file": ([_c.c_char_p, _P(vp)], _c.c_int),
+        "st_module_free": ([vp], _c.c_int),
+        "st_module_version": ([vp, _P(i32), _P(i32), _P(i32)], _c.c_int),
+        "st_module_entry_count": ([vp, _P(i32)], _c.c_int),
+        "st_module_entry": ([vp, i32, _P(StModuleEntryInfo)], _c.c_int),
+        "st_module_param": ([vp, i32, i32, _P(i32), _P(i32)], _c.c_int),
+        "st_launch_module": ([vp, vp, _c.c_char_p, _P(StGrid), _P(StParam), i32, _P(StExec)], _c.c_int),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)

@@ -107,10 +107,10 @@ def grid_from_dispatch(entry_name: str, dispatch: Sequence[int], tile_elems: int
     return (g.x, g.y, g.z)
 
 
-def run_tile_kernel(*, entry_name: str, parameter_arrays: Iterable[np.ndarray], output_indices: Iterable[int],
-                    dispatch: tuple[int, int, int] | None = None, grid: tuple[int, int, int] | None = None,
-                    tile_elems: int | None = None, device: int = 0, timeout_ms: int = 60000,
-                    spirv_path=None) -> list[np.ndarray]:
+def run_tile_kernel(*, entry_name: str | None = None, parameter_arrays: Iterable[np.ndarray],
+                    output_indices: Iterable[int], dispatch: tuple[int, int, int] | None = None,
+                    grid: tuple[int, int, int] | None = None, tile_elems: int | None = None, device: int = 0,
+                    timeout_ms: int = 60000, spirv_path=None, module=None) -> list[np.ndarray]:
     """Run a registered kernel on host arrays and return the output arrays.
 
     Same contract as run_spirv_kernel (spirv_runtime.py:153-174): every
@@ -121,6 +121,12 @@ def run_tile_kernel(*, entry_name: str, parameter_arrays: Iterable[np.ndarray], 
     workgroups; converted with ``tile_elems``, default: the entry's tile).
     ``spirv_path`` is accepted for signature compatibility and ignored: the
     kernel is found by ``entry_name`` in the native registry.
+
+    ``module`` (a .tilebc path, its bytes, or a ``TileModule``) takes the
+    place of the SPIR-V module: ``entry_name`` (optional for a one-entry
+    module) then names one of its entries, the bindings are checked against
+    that entry's parameters, the module's tile sizes are the kernel
+    constants, and ``tile_elems`` defaults to the module's tile.
     """
     arrays = [np.ascontiguousarray(a) for a in parameter_arrays]
     outs = [int(i) for i in output_indices]
@@ -139,6 +145,25 @@ def run_tile_kernel(*, entry_name: str, parameter_arrays: Iterable[np.ndarray], 
             params[i].dtype = _np_dtype_code(a)
             params[i].data = a.ctypes.data
             params[i].bytes = a.nbytes
+    out_idx = (ctypes.c_int32 * len(outs))(*outs)
+    ex = N.StExec(None, device, N.ST_EXEC_HOST_BUFFERS | N.ST_EXEC_SYNC, timeout_ms, out_idx, len(outs))
+    if module is not None:
+        from .module import TileModule
+
+        mod = module if isinstance(module, TileModule) else TileModule(module)
+        ent = mod.entry(entry_name)
+        if grid is None:
+            if dispatch is None:
+                raise ValueError("give the cuda_tile grid or the reference dispatch")
+            if tile_elems is None:
+                tile_elems = ent.tile_elems
+            if tile_elems is None or ent.backend_entry is None:
+                raise ValueError(f"entry {ent.name}: pass tile_elems or grid (the module does not fix its tile)")
+            grid = grid_from_dispatch(ent.backend_entry, dispatch, tile_elems)
+        mod.launch(context(device), ent.name, grid, params, ex)
+        return [arrays[i] for i in outs]
+    if entry_name is None:
+        raise ValueError("entry_name is required without a module")
     if grid is None:
         if dispatch is None:
             raise ValueError("give the cuda_tile grid or the reference dispatch")
@@ -146,8 +171,6 @@ def run_tile_kernel(*, entry_name: str, parameter_arrays: Iterable[np.ndarray], 
             tile_elems = _default_tile_elems(entry_name)
         grid = grid_from_dispatch(entry_name, dispatch, tile_elems)
     g = N.StGrid(*[int(x) for x in grid])
-    out_idx = (ctypes.c_int32 * len(outs))(*outs)
-    ex = N.StExec(None, device, N.ST_EXEC_HOST_BUFFERS | N.ST_EXEC_SYNC, timeout_ms, out_idx, len(outs))
     N.check(N.lib().st_launch(context(device), entry_name.encode(), ctypes.byref(g), params, len(arrays),
                               ctypes.byref(ex)), f"st_launch({entry_name})")
     return [arrays[i] for i in outs]

@@ -9,6 +9,11 @@
 // so results are compared bit for bit with a sequential CPU loop (and the
 // reference's own |diff| <= 1e-3 holds a fortiori).
 //
+// Given .tilebc paths on the command line, it also does what the
+// reference's translator front end does with a module (src/main.cpp:75-187):
+// load it, list its entries, and run each vector_add / matmul_fp32 entry
+// (st_launch_module) with the module's own tile sizes on the same inputs.
+//
 // Exit status: 0 all checks passed, 1 a mismatch or a library error, 2 no
 // CUDA device (st_init failed).
 #include <cmath>
@@ -105,9 +110,93 @@ bool matmul_test(int m, int n, int k) {
     return true;
 }
 
+// Known answers through a module entry: vector_add (a = i, b = 1000 + i) and
+// matmul_fp32 (the mod-17 / mod-13 values), with the module's tile grid.
+bool module_entry_test(const st_module *mod, const st_module_entry_info &e) {
+    const st_exec ex = {nullptr, -1, ST_EXEC_SYNC, 60000, nullptr, 0};
+    if (e.backend_entry && std::strcmp(e.backend_entry, "vector_add") == 0 && e.n_constants == 1) {
+        const uint32_t n = 4112, tile = static_cast<uint32_t>(e.constants[0]);
+        std::vector<float> a(n), b(n), c(n, 0.0f);
+        for (uint32_t i = 0; i < n; ++i) {
+            a[i] = static_cast<float>(i);
+            b[i] = static_cast<float>(1000 + i);
+        }
+        void *da = device_copy(a), *db = device_copy(b), *dc = device_copy(c);
+        if (!da || !db || !dc) return false;
+        const st_param p[9] = {buffer(da, n), i32(n), i32(1), buffer(db, n), i32(n), i32(1),
+                               buffer(dc, n), i32(n), i32(1)};
+        const st_grid grid = {(n + tile - 1) / tile, 1, 1};
+        if (!ok(st_launch_module(g_ctx, mod, e.name, &grid, p, 9, &ex), "st_launch_module(vector_add)")) return false;
+        if (!ok(st_download(g_ctx, -1, c.data(), dc, n * sizeof(float)), "st_download")) return false;
+        st_free(g_ctx, -1, da);
+        st_free(g_ctx, -1, db);
+        st_free(g_ctx, -1, dc);
+        for (uint32_t i = 0; i < n; ++i)
+            if (c[i] != a[i] + b[i]) {
+                std::fprintf(stderr, "module vector_add: c[%u] = %g, want %g\n", i, c[i], a[i] + b[i]);
+                return false;
+            }
+        std::printf("module %s tile=%u n=%u ok\n", e.name, tile, n);
+        return true;
+    }
+    if (e.backend_entry && std::strcmp(e.backend_entry, "matmul_fp32") == 0 && e.n_constants == 3) {
+        const int m = 100, n = 70, k = 33, tm = e.constants[0], tn = e.constants[1];
+        std::vector<float> a(static_cast<size_t>(m) * k), b(static_cast<size_t>(k) * n), c(static_cast<size_t>(m) * n);
+        for (size_t i = 0; i < a.size(); ++i) a[i] = static_cast<float>(static_cast<int>(i % 17) - 8) * 0.25f;
+        for (size_t i = 0; i < b.size(); ++i) b[i] = static_cast<float>(static_cast<int>(i % 13) - 6) * 0.5f;
+        void *da = device_copy(a), *db = device_copy(b), *dc = device_copy(c);
+        if (!da || !db || !dc) return false;
+        const st_param p[15] = {buffer(da, a.size()), i32(m), i32(k), i32(k), i32(1),
+                                buffer(db, b.size()), i32(k), i32(n), i32(n), i32(1),
+                                buffer(dc, c.size()), i32(m), i32(n), i32(n), i32(1)};
+        const st_grid grid = {static_cast<uint32_t>(((m + tm - 1) / tm) * ((n + tn - 1) / tn)), 1, 1};
+        if (!ok(st_launch_module(g_ctx, mod, e.name, &grid, p, 15, &ex), "st_launch_module(matmul)")) return false;
+        if (!ok(st_download(g_ctx, -1, c.data(), dc, c.size() * sizeof(float)), "st_download")) return false;
+        st_free(g_ctx, -1, da);
+        st_free(g_ctx, -1, db);
+        st_free(g_ctx, -1, dc);
+        for (int i = 0; i < m; ++i)
+            for (int j = 0; j < n; ++j) {
+                float acc = 0.0f;
+                for (int q = 0; q < k; ++q) acc += a[static_cast<size_t>(i) * k + q] * b[static_cast<size_t>(q) * n + j];
+                if (c[static_cast<size_t>(i) * n + j] != acc) {
+                    std::fprintf(stderr, "module matmul: C[%d,%d] = %g, want %g\n", i, j,
+                                 c[static_cast<size_t>(i) * n + j], acc);
+                    return false;
+                }
+            }
+        std::printf("module %s tiles=%dx%dx%d ok\n", e.name, tm, tn, e.constants[2]);
+        return true;
+    }
+    std::printf("module %s: not run by this example\n", e.name);
+    return true;
+}
+
+bool module_test(const char *path) {
+    st_module *mod = nullptr;
+    if (!ok(st_module_load_file(path, &mod), "st_module_load_file")) return false;
+    int32_t major = 0, minor = 0, count = 0;
+    st_module_version(mod, &major, &minor, nullptr);
+    st_module_entry_count(mod, &count);
+    std::printf("loaded %s: TileIR bytecode %d.%d, %d entries\n", path, major, minor, count);
+    bool all = true;
+    for (int32_t i = 0; i < count; ++i) {
+        st_module_entry_info e;
+        if (!ok(st_module_entry(mod, i, &e), "st_module_entry")) {
+            all = false;
+            continue;
+        }
+        std::printf("  entry %s: %d bindings, %d arrays, backend %s\n", e.name, e.n_params, e.n_arrays,
+                    e.backend_entry ? e.backend_entry : "(none)");
+        all = module_entry_test(mod, e) && all;
+    }
+    st_module_free(mod);
+    return all;
+}
+
 }  // namespace
 
-int main() {
+int main(int argc, char **argv) {
     std::printf("library %s\n", st_version());
     if (st_init(nullptr, 0, &g_ctx) != ST_OK) {
         std::fprintf(stderr, "no CUDA device: %s\n", st_last_error());
@@ -117,6 +206,7 @@ int main() {
     for (uint32_t n : {1024u, 2048u, 4112u}) all = vector_add_test(n) && all;
     const int shapes[4][3] = {{64, 64, 64}, {256, 256, 256}, {100, 70, 33}, {33, 129, 200}};
     for (const auto &s : shapes) all = matmul_test(s[0], s[1], s[2]) && all;
+    for (int i = 1; i < argc; ++i) all = module_test(argv[i]) && all;
     st_shutdown(g_ctx);
     std::printf(all ? "all checks passed\n" : "FAILED\n");
     return all ? 0 : 1;

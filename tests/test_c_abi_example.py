@@ -1,8 +1,8 @@
 """The reference's host-side tests (examples.cpp: run_vector_add_test,
 run_matmul_test) as a C++ program over the C ABI, with no Python in the
 loop: built with g++ against include/sptiles_b200.h and the in-tree library,
-run on the GPU (known answers, bit for bit) and, without one, checked to
-fail cleanly at st_init."""
+run on the GPU (known answers, bit for bit; also through the entries of
+cuda_tile modules) and, without one, checked to fail cleanly at st_init."""
 import shutil
 import subprocess
 from pathlib import Path
@@ -39,9 +39,13 @@ def test_example_builds_and_fails_cleanly_without_a_gpu(tmp_path):
 @pytest.mark.gpu
 def test_example_runs_the_reference_tests_on_the_gpu(tmp_path):
     exe = build(tmp_path)
-    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=300)
+    modules = [str(ROOT / "tests" / "golden" / f) for f in ("vector_add.tilebc", "vector_add2D.tilebc",
+                                                             "matmul.tilebc", "matmul_multi.tilebc")]
+    r = subprocess.run([str(exe), *modules], capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stdout + r.stderr
     out = r.stdout
     for line in ("vector_add n=1024 ok", "vector_add n=4112 ok", "matmul_fp32 64x64x64 ok",
-                 "matmul_fp32 33x129x200 ok", "all checks passed"):
+                 "matmul_fp32 33x129x200 ok", "module vector_add tile=16 n=4112 ok",
+                 "module vector_add tile=512 n=4112 ok", "module matmul_fp32 tiles=32x32x32 ok",
+                 "entry matmul_f16: 15 bindings, 3 arrays, backend matmul_f16", "all checks passed"):
         assert line in out, out
