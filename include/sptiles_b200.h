@@ -154,6 +154,17 @@ int st_launch(st_ctx *ctx, const char *entry_name, const st_grid *grid,
 int st_grid_from_dispatch(const char *entry_name, const uint32_t dispatch[3], int64_t tile_elems,
                           st_grid *out);
 
+/* ---- failure path check.  Runs one warp that waits, with the helpers the
+ * GEMM kernels' bounded waits use, on something that never completes: an
+ * mbarrier nothing arrives on (kind 0) or a GPU-scope flag nothing sets
+ * (kind 1).  After limit_us (1 .. 10^7) it gives up, records its abort code
+ * in the device's error word and returns; the next bounded host wait
+ * (ST_EXEC_SYNC here, or st_sync) reports ST_ERR_DEVICE_ABORT and clears the
+ * word, and the context stays usable.  Nothing faults or hangs.  No
+ * counterpart in the reference, whose host waits on a fence without a limit
+ * (src/examples.cpp:439). */
+int st_check_device_wait(st_ctx *ctx, int32_t kind, uint32_t limit_us, const st_exec *exec);
+
 /* ---- cuda_tile modules (TileIR bytecode, .tilebc): entry discovery.
  * Replace the translator's module loading (src/main.cpp:75-104:
  * load_cuda_tile_file, isTileIRBytecode, readBytecode) and its derivation of

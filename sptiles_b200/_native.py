@@ -37,7 +37,7 @@ EXPORTED = (
     "st_matmul_plan", "st_stream_k_split", "st_shard_range", "st_matmul_static_scratch", "st_vector_fma", "st_cast",
     "st_ipc_handle", "st_ipc_open", "st_ipc_close", "st_matmul_allgather",
     "st_module_load", "st_module_load_file", "st_module_free", "st_module_version", "st_module_entry_count",
-    "st_module_entry", "st_module_param", "st_launch_module",
+    "st_module_entry", "st_module_param", "st_launch_module", "st_check_device_wait",
 )
 
 
@@ -122,6 +122,7 @@ def _declare(L: ctypes.CDLL) -> None:
         "st_shard_range": ([i64, i32, i32, i64, _P(i64), _P(i64)], _c.c_int),
         "st_matmul_static_scratch": ([_P(StTensor), _P(StTensor), _P(StTensor), _P(StTensor), _P(StExec)],
                                      _c.c_int),
+        "st_check_device_wait": ([vp, i32, u32, _P(StExec)], _c.c_int),
         "st_module_load": ([vp, u64, _P(vp)], _c.c_int),
         "st_module_load_file": ([_c.c_char_p, _P(vp)], _c.c_int),
         "st_module_free": ([vp], _c.c_int),

@@ -18,7 +18,7 @@ PKG = Path(__file__).resolve().parent
 ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libsptiles_b200.so"
-SOURCES = ["runtime.cu", "vecadd.cu", "elementwise.cu", "gemm.cu", "pack.cu", "noalloc.cu", "module.cu"]
+SOURCES = ["runtime.cu", "vecadd.cu", "elementwise.cu", "gemm.cu", "pack.cu", "noalloc.cu", "module.cu", "diag.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

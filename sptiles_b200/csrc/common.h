@@ -87,6 +87,13 @@ constexpr int kDevAbortGemmProducer = 0x101;
 constexpr int kDevAbortGemmMma = 0x102;
 constexpr int kDevAbortGemmEpilogue = 0x103;
 constexpr int kDevAbortGemmStreamK = 0x104;  // a split tile's partial never arrived
+constexpr int kDevAbortWaitCheckBarrier = 0x1f0;  // st_check_device_wait: mbarrier wait ran out
+constexpr int kDevAbortWaitCheckFlag = 0x1f1;     // st_check_device_wait: flag poll ran out
+
+// One warp waits (bounded by limit_ns) on an mbarrier nothing arrives on
+// (kind 0) or a flag nothing sets (kind 1), then records its abort code in
+// dev_err and returns (diag.cu).
+int launch_wait_check(int kind, uint64_t limit_ns, int *dev_err, cudaStream_t stream);
 
 // ---- launchers (implemented in vecadd.cu, gemm.cu, pack.cu) ----
 

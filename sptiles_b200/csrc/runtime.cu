@@ -1132,6 +1132,18 @@ int st_vector_fma(st_ctx *ctx, const st_tensor *a, const st_tensor *b, const st_
     return finish(x);
 }
 
+int st_check_device_wait(st_ctx *ctx, int32_t kind, uint32_t limit_us, const st_exec *exec) {
+    if (kind != 0 && kind != 1)
+        return fail(ST_ERR_INVALID_ARGUMENT, "st_check_device_wait: kind must be 0 (mbarrier) or 1 (flag)");
+    if (limit_us == 0 || limit_us > 10u * 1000 * 1000)
+        return fail(ST_ERR_INVALID_ARGUMENT, "st_check_device_wait: limit_us must be in [1, 10^7]");
+    ExecCtx x;
+    ST_TRY(resolve_exec(ctx, exec, &x));
+    DeviceGuard guard(x.dev->ordinal);
+    ST_TRY(launch_wait_check(kind, static_cast<uint64_t>(limit_us) * 1000, x.dev->dev_err, x.stream));
+    return finish(x);
+}
+
 int st_cast(st_ctx *ctx, const st_tensor *a, const st_tensor *c, const st_exec *exec) {
     ExecCtx x;
     ST_TRY(resolve_exec(ctx, exec, &x));

@@ -172,3 +172,10 @@ def test_descriptors_match_reference_layout():
     assert [int(v[0]) for v in d2[1:]] == [3, 4, 4, 1]
     d1 = st.tensor_1d_descriptor(np.arange(7, dtype=np.float32))
     assert [int(v[0]) for v in d1[1:]] == [7, 1]
+
+
+def test_device_wait_check_rejects_bad_arguments_before_device_work():
+    ex = N.StExec(None, 0, N.ST_EXEC_SYNC, 1000, None, 0)
+    for kind, limit in ((2, 1000), (-1, 1000), (0, 0), (1, 10_000_001)):
+        assert N.lib().st_check_device_wait(None, kind, limit, ctypes.byref(ex)) == N.ST_ERR_INVALID_ARGUMENT
+        assert "st_check_device_wait" in N.last_error()
