@@ -58,6 +58,12 @@ extern "C" {
 #define ST_EXEC_HOST_BUFFERS 2  /* st_launch only: buffer params are host memory */
 #define ST_EXEC_DETERMINISTIC 4 /* matmul: the same inputs give the same bits on every run (split tiles
                                    with fp32 C are folded in a fixed order instead of by L2 adds) */
+#define ST_EXEC_ALL_DEVICES 8   /* st_vector_add_host / st_matmul_host: the single-box partitioner in one
+                                   process -- the call is split over every device of the context
+                                   (vector_add by element ranges on 16-byte boundaries, matmul by 128-row
+                                   blocks of A and C, B and the bias to every device), each on the
+                                   context's own stream (exec->stream NULL, exec->device -1); returns
+                                   when all devices are done (bounded by timeout_ms each) */
 
 typedef struct st_ctx st_ctx;
 
@@ -108,7 +114,10 @@ int st_device_count(int32_t *count);
 int st_kernel_launches(uint64_t *count);
 
 /* ---- context: replaces create_vulkan_context / destroy_vulkan_context ---- */
-/* devices: CUDA ordinals to use (NULL with n_devices 0 = device 0). */
+/* devices: CUDA ordinals to use (NULL with n_devices 0 = device 0).  With
+ * several devices, peer access between them is enabled (NVLink), so a
+ * device's kernels may store into another's memory (st_matmul_allgather
+ * with the other devices' copies of C as peers, in one process). */
 int st_init(const int32_t *devices, int32_t n_devices, st_ctx **out);
 int st_shutdown(st_ctx *ctx);
 /* Bounded wait for all work the context issued on `device`; returns

@@ -12,7 +12,7 @@ from .api import (  # noqa: F401
     spirv_matmul, spirv_vector_add, tensor_view, vector_add, vector_fma,
 )
 from .runtime import (  # noqa: F401
-    LOCAL_SIZE_X, ceil_div, context, device_count, grid_from_dispatch, kernel_launches, matmul_plan,
+    LOCAL_SIZE_X, ceil_div, context, context_group, device_count, grid_from_dispatch, kernel_launches, matmul_plan,
     run_tile_kernel,
     shard_range, shutdown, stream_k_split, sync, tensor_1d_descriptor, tensor_2d_descriptor, tile_raster,
 )

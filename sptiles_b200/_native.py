@@ -27,7 +27,7 @@ ST_ERR_DEVICE_ABORT = 8
 ST_F32, ST_F16, ST_BF16, ST_I32 = 0, 1, 2, 3
 ST_PARAM_BUFFER, ST_PARAM_I32 = 0, 1
 ST_MODULE_PARAM_BUFFER, ST_MODULE_PARAM_I32, ST_MODULE_PARAM_OTHER = 0, 1, 2
-ST_EXEC_SYNC, ST_EXEC_HOST_BUFFERS, ST_EXEC_DETERMINISTIC = 1, 2, 4
+ST_EXEC_SYNC, ST_EXEC_HOST_BUFFERS, ST_EXEC_DETERMINISTIC, ST_EXEC_ALL_DEVICES = 1, 2, 4, 8
 
 # Every symbol the header declares; the CPU test suite checks the library exports them all.
 EXPORTED = (

@@ -19,11 +19,12 @@ from __future__ import annotations
 import ctypes
 import struct
 from pathlib import Path
+from typing import Sequence
 
 import torch
 
 from . import _native as N
-from .runtime import context
+from .runtime import context, context_group
 
 VECTOR_ADD_TILE_SIZE = 16  # spirv_vector_add.py:27
 MATMUL_TILE_M = 32  # spirv_matmul.py:27
@@ -80,6 +81,11 @@ def _ctx(ex: N.StExec) -> int:
     return context(ex.device)
 
 
+def _all_devices_exec() -> N.StExec:
+    """st_exec of a call split over every device of its context (each on the context's stream)."""
+    return N.StExec(None, -1, N.ST_EXEC_ALL_DEVICES | _det_flag(), 60000, None, 0)
+
+
 # ----------------------------------------------------------------- lean calls
 # CUDA tensors go to the same C ABI entry points with their st_tensor and
 # st_exec descriptors packed by struct -- one C-level call per descriptor
@@ -123,8 +129,13 @@ def _exec_desc(device: int) -> bytes:
 
 
 # ----------------------------------------------------------------- vector add
-def vector_add(A: torch.Tensor, B: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
-    """C = A + B (f32, rank 1 or 2, any strides), bit-exact IEEE adds."""
+def vector_add(A: torch.Tensor, B: torch.Tensor, out: torch.Tensor | None = None, *,
+               devices: Sequence[int] | None = None) -> torch.Tensor:
+    """C = A + B (f32, rank 1 or 2, any strides), bit-exact IEEE adds.
+
+    ``devices`` (host tensors only): split the add over those GPUs by element
+    ranges, in this process (ST_EXEC_ALL_DEVICES).
+    """
     if A.shape != B.shape:
         raise ValueError(f"Input tensors must have the same shape: {A.shape} != {B.shape}")
     dev = A.get_device()
@@ -132,6 +143,14 @@ def vector_add(A: torch.Tensor, B: torch.Tensor, out: torch.Tensor | None = None
         raise ValueError("Input tensors must be on the same torch device.")
     C = out if out is not None else torch.empty(A.shape, dtype=A.dtype, device=A.device,
                                                  pin_memory=A.device.type == "cpu" and A.is_pinned())
+    if devices is not None:
+        if dev >= 0:
+            raise ValueError("devices= splits calls on host tensors; CUDA tensors run on their own device")
+        va, vb, vc = tensor_view(A), tensor_view(B), tensor_view(C)
+        ex = _all_devices_exec()
+        N.check(N.lib().st_vector_add_host(context_group(devices), ctypes.byref(va), ctypes.byref(vb),
+                                           ctypes.byref(vc), ctypes.byref(ex)), "vector_add")
+        return C
     if dev >= 0:
         rc = _lean_fn("st_vector_add", 4)(context(dev), _desc(A), _desc(B), _desc(C), _exec_desc(dev))
         if rc != N.ST_OK:
@@ -204,12 +223,15 @@ def cast(A: torch.Tensor, dtype: torch.dtype, out: torch.Tensor | None = None) -
 
 # ----------------------------------------------------------------- matmul
 def matmul(A: torch.Tensor, B: torch.Tensor, bias: torch.Tensor | None = None, *,
-           out_dtype: torch.dtype | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+           out_dtype: torch.dtype | None = None, out: torch.Tensor | None = None,
+           devices: Sequence[int] | None = None) -> torch.Tensor:
     """C = A @ B (+ bias) with fp32 accumulation on the tensor cores.
 
     A, B: both float32 (3xTF32), both float16 or both bfloat16.  C defaults
     to A's dtype (matmul.py:245); ``out_dtype`` may ask for float32, float16
-    or bfloat16.  bias (length N) is float32 or A's dtype.
+    or bfloat16.  bias (length N) is float32 or A's dtype.  ``devices`` (host
+    tensors only): split the call over those GPUs by 128-row blocks of A and
+    C, in this process (ST_EXEC_ALL_DEVICES).
     """
     sa, sb = A.shape, B.shape
     if len(sa) != 2 or len(sb) != 2:
@@ -225,6 +247,15 @@ def matmul(A: torch.Tensor, B: torch.Tensor, bias: torch.Tensor | None = None, *
     if out is None:
         out = torch.empty((sa[0], sb[1]), dtype=out_dtype or A.dtype, device=A.device,
                           pin_memory=dev < 0 and A.device.type == "cpu" and A.is_pinned())
+    if devices is not None:
+        if dev >= 0:
+            raise ValueError("devices= splits calls on host tensors; CUDA tensors run on their own device")
+        va, vb, vc = tensor_view(A), tensor_view(B), tensor_view(out)
+        vbias = ctypes.byref(tensor_view(bias)) if bias is not None else None
+        ex = _all_devices_exec()
+        N.check(N.lib().st_matmul_host(context_group(devices), ctypes.byref(va), ctypes.byref(vb), vbias,
+                                       ctypes.byref(vc), ctypes.byref(ex)), "matmul")
+        return out
     if dev >= 0:
         rc = _lean_fn("st_matmul", 5)(context(dev), _desc(A), _desc(B), None if bias is None else _desc(bias),
                                       _desc(out), _exec_desc(dev))

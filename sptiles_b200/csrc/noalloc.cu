@@ -40,8 +40,8 @@ namespace {
 constexpr size_t kStaticScratchBytes = size_t(ST_STATIC_SCRATCH_BYTES);
 constexpr uint64_t kWaitLimitNs = 4ull * 1000 * 1000 * 1000;
 
-__device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
-__device__ int g_static_abort;
+static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
+static __device__ int g_static_abort;
 
 struct StaticDevice {
     bool ready = false;

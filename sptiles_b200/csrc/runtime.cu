@@ -592,7 +592,7 @@ int copy_block_out(cudaStream_t s, const st_tensor &h, const void *dev, int64_t 
 // copies use row pitches rounded up to 8 elements, so every block view is a
 // 16-byte-aligned TMA operand.
 int matmul_host_pipelined(const ExecCtx &x, const st_tensor &a, const st_tensor &b, const st_tensor *bias,
-                          const st_tensor &c) {
+                          const st_tensor &c, bool wait) {
     DeviceState *d = x.dev;
     ST_TRY(ensure_copy_streams(d));
     const int64_t M = a.shape[0], K = a.shape[1], N = b.shape[1];
@@ -656,12 +656,12 @@ int matmul_host_pipelined(const ExecCtx &x, const st_tensor &a, const st_tensor 
     }
     ST_TRY(stream_after(d, ev, x.stream, d->copy_out));
     ST_TRY(ws_release(d->stage, x.stream));
-    return bounded_sync(d, x.stream, x.timeout_ms);
+    return wait ? bounded_sync(d, x.stream, x.timeout_ms) : ST_OK;
 }
 
 // C = A + B on dense host arrays, in element chunks over the three streams.
 int vector_add_host_pipelined(const ExecCtx &x, const st_tensor &a, const st_tensor &b, const st_tensor &c,
-                              int64_t n) {
+                              int64_t n, bool wait) {
     DeviceState *d = x.dev;
     ST_TRY(ensure_copy_streams(d));
     const size_t bytes = static_cast<size_t>(n) * 4;
@@ -688,7 +688,130 @@ int vector_add_host_pipelined(const ExecCtx &x, const st_tensor &a, const st_ten
     }
     ST_TRY(stream_after(d, ev, x.stream, d->copy_out));
     ST_TRY(ws_release(d->stage, x.stream));
-    return bounded_sync(d, x.stream, x.timeout_ms);
+    return wait ? bounded_sync(d, x.stream, x.timeout_ms) : ST_OK;
+}
+
+// ------------------------------------------------------------ host-memory calls on one device
+// Dense arrays of one layout: the add runs over one flat range.
+bool vector_add_host_flat(const st_tensor &a, const st_tensor &b, const st_tensor &c) {
+    bool flat = true;
+    for (const st_tensor *t : {&a, &b, &c}) {
+        if (t->rank == 1) flat &= t->shape[0] <= 1 || t->strides[0] == 1;
+        else flat &= (t->shape[1] <= 1 || t->strides[1] == 1) && (t->shape[0] <= 1 || t->strides[0] == t->shape[1]);
+    }
+    return flat;
+}
+
+// C = A + B on host memory through the device of `x`; waits (bounded) when `wait`.
+int vector_add_host_one(const ExecCtx &x, const st_tensor &a, const st_tensor &b, const st_tensor &c, bool wait) {
+    int64_t n = 1;
+    for (int i = 0; i < c.rank; ++i) n *= c.shape[i];
+    if (vector_add_host_flat(a, b, c) && n > 0) return vector_add_host_pipelined(x, a, b, c, n, wait);
+    void *base = nullptr;
+    ST_TRY(ws_acquire(x.dev->stage, staged_bytes(a) + staged_bytes(b) + staged_bytes(c), x.stream, &base));
+    uint8_t *cursor = static_cast<uint8_t *>(base);
+    st_tensor da, db, dc;
+    ST_TRY(stage_in(x, a, cursor, &da));
+    ST_TRY(stage_in(x, b, cursor, &db));
+    dc = c;
+    dc.data = cursor;
+    if (c.rank == 1) dc.strides[0] = 1;
+    else {
+        dc.strides[0] = c.shape[1];
+        dc.strides[1] = 1;
+    }
+    const int64_t rows = c.rank == 2 ? c.shape[0] : 1;
+    const int64_t cols = c.rank == 2 ? c.shape[1] : c.shape[0];
+    ST_TRY(vector_add_views(x, da, db, dc, rows, cols));
+    ST_TRY(stage_out(x, dc, c));
+    ST_TRY(ws_release(x.dev->stage, x.stream));
+    return wait ? bounded_sync(x.dev, x.stream, x.timeout_ms) : ST_OK;
+}
+
+// C = A @ B (+ bias) on host memory through the device of `x`; waits (bounded) when `wait`.
+int matmul_host_one(const ExecCtx &x, const st_tensor &a, const st_tensor &b, const st_tensor *bias,
+                    const st_tensor &c, bool wait) {
+    // 16-bit operands with unit column strides: chunked and overlapped (the
+    // fp32 path packs B once per call, so it stays unchunked)
+    if (a.dtype != ST_F32 && a.shape[0] > 0 && b.shape[1] > 0 && a.shape[1] > 0 && host_rows_dense(a) &&
+        host_rows_dense(b) && host_rows_dense(c))
+        return matmul_host_pipelined(x, a, b, bias, c, wait);
+    size_t need = staged_bytes(a) + staged_bytes(b) + staged_bytes(c) + (bias ? staged_bytes(*bias) : 0);
+    void *base = nullptr;
+    ST_TRY(ws_acquire(x.dev->stage, need, x.stream, &base));
+    uint8_t *cursor = static_cast<uint8_t *>(base);
+    st_tensor da, db, dbias, dc;
+    ST_TRY(stage_in(x, a, cursor, &da));
+    ST_TRY(stage_in(x, b, cursor, &db));
+    if (bias) ST_TRY(stage_in(x, *bias, cursor, &dbias));
+    dc = c;
+    dc.data = cursor;
+    dc.strides[0] = c.shape[1];
+    dc.strides[1] = 1;
+    ST_TRY(matmul_device(x, da, db, bias ? &dbias : nullptr, dc));
+    ST_TRY(stage_out(x, dc, c));
+    ST_TRY(ws_release(x.dev->stage, x.stream));
+    return wait ? bounded_sync(x.dev, x.stream, x.timeout_ms) : ST_OK;
+}
+
+// ------------------------------------------------------------ single-box partitioner (one process)
+// ST_EXEC_ALL_DEVICES: each device runs on its own stream of the context.
+int check_all_devices(const st_exec *exec) {
+    if (exec->stream != nullptr)
+        return fail(ST_ERR_INVALID_ARGUMENT,
+                    "ST_EXEC_ALL_DEVICES runs every device on the context's own stream: exec->stream must be NULL");
+    if (exec->device >= 0)
+        return fail(ST_ERR_INVALID_ARGUMENT, "ST_EXEC_ALL_DEVICES uses every device: exec->device must be -1");
+    return ST_OK;
+}
+
+// Rows [r0, r1) of a host view (elements, for rank 1).
+st_tensor host_rows(const st_tensor &t, int64_t r0, int64_t r1) {
+    st_tensor v = t;
+    v.data = static_cast<uint8_t *>(t.data) + static_cast<size_t>(r0 * t.strides[0]) * dtype_size(t.dtype);
+    v.shape[0] = r1 - r0;
+    return v;
+}
+
+// Elements [e0, e1) of a dense host array, as a rank-1 view.
+st_tensor flat_range(const st_tensor &t, int64_t e0, int64_t e1) {
+    st_tensor v = t;
+    v.data = static_cast<uint8_t *>(t.data) + static_cast<size_t>(e0) * dtype_size(t.dtype);
+    v.rank = 1;
+    v.shape[0] = e1 - e0;
+    v.strides[0] = 1;
+    v.shape[1] = 0;
+    v.strides[1] = 0;
+    return v;
+}
+
+// Split [0, total) into one contiguous range per device of the context
+// (boundaries on multiples of `align`, as st_shard_range), enqueue each
+// range's work on its device, then wait (bounded) for every device that got
+// work -- also after a failure, so that nothing is left in flight.
+template <typename Enqueue>
+int for_each_device_shard(st_ctx *ctx, const ExecCtx &x0, int64_t total, int64_t align, Enqueue enqueue) {
+    const int g_count = static_cast<int>(ctx->devs.size());
+    const int64_t units = cdiv(total, align);
+    std::vector<ExecCtx> busy;
+    int rc = ST_OK;
+    for (int g = 0; g < g_count && rc == ST_OK; ++g) {
+        const int64_t b = std::min(units * g / g_count * align, total);
+        const int64_t e = std::min(units * (g + 1) / g_count * align, total);
+        if (e <= b) continue;
+        ExecCtx xg = x0;
+        xg.dev = &ctx->devs[g];
+        xg.stream = xg.dev->stream;
+        DeviceGuard guard(xg.dev->ordinal);
+        rc = enqueue(xg, b, e);
+        busy.push_back(xg);
+    }
+    for (const ExecCtx &xg : busy) {
+        DeviceGuard guard(xg.dev->ordinal);
+        const int r = bounded_sync(xg.dev, xg.stream, xg.timeout_ms);
+        if (rc == ST_OK) rc = r;
+    }
+    return rc;
 }
 
 // ------------------------------------------------------------ entry registry
@@ -943,6 +1066,18 @@ int st_init(const int32_t *devices, int32_t n_devices, st_ctx **out) {
         }
         ctx->devs.push_back(d);
     }
+    // peer access between the context's devices (NVLink), for peer copies and
+    // for GEMM epilogues that store into another device's copy of C
+    for (int i : ords)
+        for (int j : ords) {
+            int can = 0;
+            if (i == j || cudaDeviceCanAccessPeer(&can, i, j) != cudaSuccess || !can) {
+                cudaGetLastError();
+                continue;
+            }
+            DeviceGuard guard(i);
+            if (cudaDeviceEnablePeerAccess(j, 0) != cudaSuccess) cudaGetLastError();  // already enabled is fine
+        }
     *out = ctx;
     return ST_OK;
 }
@@ -1169,37 +1304,23 @@ int st_vector_add_host(st_ctx *ctx, const st_tensor *a, const st_tensor *b, cons
     ExecCtx x;
     ST_TRY(resolve_exec(ctx, exec, &x));
     ST_TRY(check_vector_add(a, b, c));
-    DeviceGuard guard(x.dev->ordinal);
-    {
-        // dense arrays of the same layout: one flat range, pipelined
-        bool flat = true;
-        int64_t n = 1;
-        for (const st_tensor *t : {a, b, c}) {
-            if (t->rank == 1) flat &= t->shape[0] <= 1 || t->strides[0] == 1;
-            else flat &= (t->shape[1] <= 1 || t->strides[1] == 1) && (t->shape[0] <= 1 || t->strides[0] == t->shape[1]);
+    if (x.flags & ST_EXEC_ALL_DEVICES) {
+        ST_TRY(check_all_devices(exec));
+        if (vector_add_host_flat(*a, *b, *c)) {  // element ranges on 16-byte boundaries
+            int64_t n = 1;
+            for (int i = 0; i < c->rank; ++i) n *= c->shape[i];
+            return for_each_device_shard(ctx, x, n, 4, [&](const ExecCtx &xg, int64_t e0, int64_t e1) {
+                return vector_add_host_one(xg, flat_range(*a, e0, e1), flat_range(*b, e0, e1),
+                                           flat_range(*c, e0, e1), false);
+            });
         }
-        for (int i = 0; i < c->rank; ++i) n *= c->shape[i];
-        if (flat && n > 0) return vector_add_host_pipelined(x, *a, *b, *c, n);
+        return for_each_device_shard(ctx, x, c->shape[0], 1, [&](const ExecCtx &xg, int64_t r0, int64_t r1) {
+            return vector_add_host_one(xg, host_rows(*a, r0, r1), host_rows(*b, r0, r1), host_rows(*c, r0, r1),
+                                       false);
+        });
     }
-    void *base = nullptr;
-    ST_TRY(ws_acquire(x.dev->stage, staged_bytes(*a) + staged_bytes(*b) + staged_bytes(*c), x.stream, &base));
-    uint8_t *cursor = static_cast<uint8_t *>(base);
-    st_tensor da, db, dc;
-    ST_TRY(stage_in(x, *a, cursor, &da));
-    ST_TRY(stage_in(x, *b, cursor, &db));
-    dc = *c;
-    dc.data = cursor;
-    if (c->rank == 1) dc.strides[0] = 1;
-    else {
-        dc.strides[0] = c->shape[1];
-        dc.strides[1] = 1;
-    }
-    const int64_t rows = c->rank == 2 ? c->shape[0] : 1;
-    const int64_t cols = c->rank == 2 ? c->shape[1] : c->shape[0];
-    ST_TRY(vector_add_views(x, da, db, dc, rows, cols));
-    ST_TRY(stage_out(x, dc, *c));
-    ST_TRY(ws_release(x.dev->stage, x.stream));
-    return bounded_sync(x.dev, x.stream, x.timeout_ms);
+    DeviceGuard guard(x.dev->ordinal);
+    return vector_add_host_one(x, *a, *b, *c, true);
 }
 
 int st_matmul_host(st_ctx *ctx, const st_tensor *a, const st_tensor *b, const st_tensor *bias, const st_tensor *c,
@@ -1207,28 +1328,15 @@ int st_matmul_host(st_ctx *ctx, const st_tensor *a, const st_tensor *b, const st
     ExecCtx x;
     ST_TRY(resolve_exec(ctx, exec, &x));
     ST_TRY(check_matmul(a, b, bias, c));
+    if (x.flags & ST_EXEC_ALL_DEVICES) {
+        ST_TRY(check_all_devices(exec));
+        // M-row blocks of 128: each device gets its rows of A and C, all of B and the bias
+        return for_each_device_shard(ctx, x, a->shape[0], 128, [&](const ExecCtx &xg, int64_t r0, int64_t r1) {
+            return matmul_host_one(xg, host_rows(*a, r0, r1), *b, bias, host_rows(*c, r0, r1), false);
+        });
+    }
     DeviceGuard guard(x.dev->ordinal);
-    // 16-bit operands with unit column strides: chunked and overlapped (the
-    // fp32 path packs B once per call, so it stays unchunked)
-    if (a->dtype != ST_F32 && a->shape[0] > 0 && b->shape[1] > 0 && a->shape[1] > 0 && host_rows_dense(*a) &&
-        host_rows_dense(*b) && host_rows_dense(*c))
-        return matmul_host_pipelined(x, *a, *b, bias, *c);
-    size_t need = staged_bytes(*a) + staged_bytes(*b) + staged_bytes(*c) + (bias ? staged_bytes(*bias) : 0);
-    void *base = nullptr;
-    ST_TRY(ws_acquire(x.dev->stage, need, x.stream, &base));
-    uint8_t *cursor = static_cast<uint8_t *>(base);
-    st_tensor da, db, dbias, dc;
-    ST_TRY(stage_in(x, *a, cursor, &da));
-    ST_TRY(stage_in(x, *b, cursor, &db));
-    if (bias) ST_TRY(stage_in(x, *bias, cursor, &dbias));
-    dc = *c;
-    dc.data = cursor;
-    dc.strides[0] = c->shape[1];
-    dc.strides[1] = 1;
-    ST_TRY(matmul_device(x, da, db, bias ? &dbias : nullptr, dc));
-    ST_TRY(stage_out(x, dc, *c));
-    ST_TRY(ws_release(x.dev->stage, x.stream));
-    return bounded_sync(x.dev, x.stream, x.timeout_ms);
+    return matmul_host_one(x, *a, *b, bias, *c, true);
 }
 
 int st_ipc_handle(st_ctx *ctx, int32_t device, void *ptr, uint8_t handle[64]) {

@@ -54,10 +54,33 @@ def context(device: int = 0) -> int:
     return ctx
 
 
+_group_contexts: dict[tuple[int, ...], int] = {}
+
+
+def context_group(devices: Sequence[int]) -> int:
+    """A process-wide native context over several CUDA devices (created on
+    first use; peer access between them is enabled), for calls split over
+    all of them (ST_EXEC_ALL_DEVICES)."""
+    key = tuple(int(d) for d in devices)
+    if not key:
+        raise ValueError("devices must name at least one CUDA device")
+    ctx = _group_contexts.get(key)
+    if ctx is None:
+        handle = ctypes.c_void_p()
+        devs = (ctypes.c_int32 * len(key))(*key)
+        N.check(N.lib().st_init(devs, len(key), ctypes.byref(handle)), f"st_init(devices {key})")
+        ctx = handle.value
+        _group_contexts[key] = ctx
+    return ctx
+
+
 def shutdown() -> None:
     for dev, ctx in list(_contexts.items()):
         N.lib().st_shutdown(ctx)
         del _contexts[dev]
+    for key, ctx in list(_group_contexts.items()):
+        N.lib().st_shutdown(ctx)
+        del _group_contexts[key]
 
 
 atexit.register(shutdown)

@@ -9,6 +9,9 @@
 // so results are compared bit for bit with a sequential CPU loop (and the
 // reference's own |diff| <= 1e-3 holds a fortiori).
 //
+// It then splits host-memory calls over every visible device in one process
+// (the single-box partitioner, ST_EXEC_ALL_DEVICES).
+//
 // Given .tilebc paths on the command line, it also does what the
 // reference's translator front end does with a module (src/main.cpp:75-187):
 // load it, list its entries, and run each vector_add / matmul_fp32 entry
@@ -172,6 +175,60 @@ bool module_entry_test(const st_module *mod, const st_module_entry_info &e) {
     return true;
 }
 
+// The single-box partitioner in one process: a context over every visible
+// device, host-memory calls split across them (ST_EXEC_ALL_DEVICES).
+bool partitioner_test() {
+    int32_t count = 0;
+    if (!ok(st_device_count(&count), "st_device_count") || count < 1) return false;
+    std::vector<int32_t> devs(count);
+    for (int32_t i = 0; i < count; ++i) devs[i] = i;
+    st_ctx *all = nullptr;
+    if (!ok(st_init(devs.data(), count, &all), "st_init(all devices)")) return false;
+    const st_exec ex = {nullptr, -1, ST_EXEC_ALL_DEVICES, 60000, nullptr, 0};
+    bool good = true;
+    {  // matmul_fp32 known answer, ragged: rows in 128-row blocks per device
+        const int m = 1000, n = 700, k = 333;
+        std::vector<float> a(static_cast<size_t>(m) * k), b(static_cast<size_t>(k) * n), c(static_cast<size_t>(m) * n);
+        for (size_t i = 0; i < a.size(); ++i) a[i] = static_cast<float>(static_cast<int>(i % 17) - 8) * 0.25f;
+        for (size_t i = 0; i < b.size(); ++i) b[i] = static_cast<float>(static_cast<int>(i % 13) - 6) * 0.5f;
+        const st_tensor ta = {a.data(), ST_F32, 2, {m, k}, {k, 1}};
+        const st_tensor tb = {b.data(), ST_F32, 2, {k, n}, {n, 1}};
+        const st_tensor tc = {c.data(), ST_F32, 2, {m, n}, {n, 1}};
+        good = ok(st_matmul_host(all, &ta, &tb, nullptr, &tc, &ex), "st_matmul_host(all devices)");
+        for (int i = 0; good && i < m; ++i)
+            for (int j = 0; good && j < n; ++j) {
+                float acc = 0.0f;
+                for (int q = 0; q < k; ++q) acc += a[static_cast<size_t>(i) * k + q] * b[static_cast<size_t>(q) * n + j];
+                if (c[static_cast<size_t>(i) * n + j] != acc) {
+                    std::fprintf(stderr, "partitioner matmul: C[%d,%d] = %g, want %g\n", i, j,
+                                 c[static_cast<size_t>(i) * n + j], acc);
+                    good = false;
+                }
+            }
+        if (good) std::printf("partitioner matmul_fp32 %dx%dx%d on %d devices ok\n", m, n, k, count);
+    }
+    if (good) {  // vector_add by element ranges
+        const int64_t n = 1000003;
+        std::vector<float> a(n), b(n), c(n, 0.0f);
+        for (int64_t i = 0; i < n; ++i) {
+            a[i] = static_cast<float>(i);
+            b[i] = static_cast<float>(1000 + i);
+        }
+        const st_tensor ta = {a.data(), ST_F32, 1, {n, 0}, {1, 0}};
+        const st_tensor tb = {b.data(), ST_F32, 1, {n, 0}, {1, 0}};
+        const st_tensor tc = {c.data(), ST_F32, 1, {n, 0}, {1, 0}};
+        good = ok(st_vector_add_host(all, &ta, &tb, &tc, &ex), "st_vector_add_host(all devices)");
+        for (int64_t i = 0; good && i < n; ++i)
+            if (c[i] != a[i] + b[i]) {
+                std::fprintf(stderr, "partitioner vector_add: c[%lld] = %g\n", static_cast<long long>(i), c[i]);
+                good = false;
+            }
+        if (good) std::printf("partitioner vector_add n=%lld on %d devices ok\n", static_cast<long long>(n), count);
+    }
+    st_shutdown(all);
+    return good;
+}
+
 bool module_test(const char *path) {
     st_module *mod = nullptr;
     if (!ok(st_module_load_file(path, &mod), "st_module_load_file")) return false;
@@ -208,6 +265,7 @@ int main(int argc, char **argv) {
     for (const auto &s : shapes) all = matmul_test(s[0], s[1], s[2]) && all;
     for (int i = 1; i < argc; ++i) all = module_test(argv[i]) && all;
     st_shutdown(g_ctx);
+    all = partitioner_test() && all;
     std::printf(all ? "all checks passed\n" : "FAILED\n");
     return all ? 0 : 1;
 }

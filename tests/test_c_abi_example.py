@@ -47,5 +47,7 @@ def test_example_runs_the_reference_tests_on_the_gpu(tmp_path):
     for line in ("vector_add n=1024 ok", "vector_add n=4112 ok", "matmul_fp32 64x64x64 ok",
                  "matmul_fp32 33x129x200 ok", "module vector_add tile=16 n=4112 ok",
                  "module vector_add tile=512 n=4112 ok", "module matmul_fp32 tiles=32x32x32 ok",
-                 "entry matmul_f16: 15 bindings, 3 arrays, backend matmul_f16", "all checks passed"):
+                 "entry matmul_f16: 15 bindings, 3 arrays, backend matmul_f16",
+                 f"partitioner matmul_fp32 1000x700x333 on {torch.cuda.device_count()} devices ok",
+                 f"partitioner vector_add n=1000003 on {torch.cuda.device_count()} devices ok", "all checks passed"):
         assert line in out, out
