@@ -229,7 +229,13 @@ struct ExecCtx {
     int flags = 0;
 };
 
-int resolve_exec(st_ctx *ctx, const st_exec *exec, ExecCtx *out) {
+// `split_ok`: the call implements ST_EXEC_ALL_DEVICES (the host-memory
+// vector_add and matmul); every other entry point refuses the flag rather
+// than running on one device only.
+int resolve_exec(st_ctx *ctx, const st_exec *exec, ExecCtx *out, bool split_ok = false) {
+    if (exec && (exec->flags & ST_EXEC_ALL_DEVICES) && !split_ok)
+        return fail(ST_ERR_INVALID_ARGUMENT,
+                    "ST_EXEC_ALL_DEVICES applies to st_vector_add_host and st_matmul_host only");
     const int device = exec ? exec->device : -1;
     ST_TRY(get_dev(ctx, device, &out->dev));
     out->stream = (exec && exec->stream) ? static_cast<cudaStream_t>(exec->stream) : out->dev->stream;
@@ -1302,7 +1308,7 @@ int st_cast(st_ctx *ctx, const st_tensor *a, const st_tensor *c, const st_exec *
 
 int st_vector_add_host(st_ctx *ctx, const st_tensor *a, const st_tensor *b, const st_tensor *c, const st_exec *exec) {
     ExecCtx x;
-    ST_TRY(resolve_exec(ctx, exec, &x));
+    ST_TRY(resolve_exec(ctx, exec, &x, true));
     ST_TRY(check_vector_add(a, b, c));
     if (x.flags & ST_EXEC_ALL_DEVICES) {
         ST_TRY(check_all_devices(exec));
@@ -1326,7 +1332,7 @@ int st_vector_add_host(st_ctx *ctx, const st_tensor *a, const st_tensor *b, cons
 int st_matmul_host(st_ctx *ctx, const st_tensor *a, const st_tensor *b, const st_tensor *bias, const st_tensor *c,
                    const st_exec *exec) {
     ExecCtx x;
-    ST_TRY(resolve_exec(ctx, exec, &x));
+    ST_TRY(resolve_exec(ctx, exec, &x, true));
     ST_TRY(check_matmul(a, b, bias, c));
     if (x.flags & ST_EXEC_ALL_DEVICES) {
         ST_TRY(check_all_devices(exec));

@@ -179,3 +179,18 @@ def test_device_wait_check_rejects_bad_arguments_before_device_work():
     for kind, limit in ((2, 1000), (-1, 1000), (0, 0), (1, 10_000_001)):
         assert N.lib().st_check_device_wait(None, kind, limit, ctypes.byref(ex)) == N.ST_ERR_INVALID_ARGUMENT
         assert "st_check_device_wait" in N.last_error()
+
+
+def test_all_devices_flag_is_refused_where_it_does_not_apply():
+    ex = N.StExec(None, -1, N.ST_EXEC_ALL_DEVICES, 1000, None, 0)
+    t = N.StTensor()
+    g = N.StGrid(1, 1, 1)
+    calls = [
+        lambda: N.lib().st_vector_add(None, ctypes.byref(t), ctypes.byref(t), ctypes.byref(t), ctypes.byref(ex)),
+        lambda: N.lib().st_matmul(None, ctypes.byref(t), ctypes.byref(t), None, ctypes.byref(t), ctypes.byref(ex)),
+        lambda: N.lib().st_launch(None, b"vector_add", ctypes.byref(g), None, 0, ctypes.byref(ex)),
+        lambda: N.lib().st_cast(None, ctypes.byref(t), ctypes.byref(t), ctypes.byref(ex)),
+    ]
+    for call in calls:
+        assert call() == N.ST_ERR_INVALID_ARGUMENT
+        assert "ST_EXEC_ALL_DEVICES applies to" in N.last_error()

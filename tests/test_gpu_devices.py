@@ -64,11 +64,11 @@ def test_vector_add_host_split_flat_and_strided():
     y = rng.uniform(-1, 1, n).astype(np.float32)
     C = st.vector_add(torch.from_numpy(x), torch.from_numpy(y), devices=ALL)
     assert C.numpy().tobytes() == (x + y).tobytes()
-    # transposed host views: rows are split instead of elements
-    a = rng.uniform(-1, 1, (300, 700)).astype(np.float32)
-    b = rng.uniform(-1, 1, (300, 700)).astype(np.float32)
-    C = st.vector_add(torch.from_numpy(a).t(), torch.from_numpy(b).t(), devices=ALL)
-    assert C.numpy().tobytes() == np.ascontiguousarray((a + b).T).tobytes()
+    # row-padded host views (pitch 800, 700 columns): rows are split instead of elements
+    a = rng.uniform(-1, 1, (300, 800)).astype(np.float32)
+    b = rng.uniform(-1, 1, (300, 800)).astype(np.float32)
+    C = st.vector_add(torch.from_numpy(a)[:, :700], torch.from_numpy(b)[:, :700], devices=ALL)
+    assert C.numpy().tobytes() == np.ascontiguousarray((a + b)[:, :700]).tobytes()
 
 
 def test_all_devices_runs_on_the_contexts_streams():
