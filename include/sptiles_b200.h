@@ -58,12 +58,14 @@ extern "C" {
 #define ST_EXEC_HOST_BUFFERS 2  /* st_launch only: buffer params are host memory */
 #define ST_EXEC_DETERMINISTIC 4 /* matmul: the same inputs give the same bits on every run (split tiles
                                    with fp32 C are folded in a fixed order instead of by L2 adds) */
-#define ST_EXEC_ALL_DEVICES 8   /* st_vector_add_host / st_matmul_host: the single-box partitioner in one
-                                   process -- the call is split over every device of the context
-                                   (vector_add by element ranges on 16-byte boundaries, matmul by 128-row
-                                   blocks of A and C, B and the bias to every device), each on the
-                                   context's own stream (exec->stream NULL, exec->device -1); returns
-                                   when all devices are done (bounded by timeout_ms each) */
+#define ST_EXEC_ALL_DEVICES 8   /* st_vector_add_host / st_matmul_host, and st_launch with
+                                   ST_EXEC_HOST_BUFFERS for the vector_add and matmul entries: the
+                                   single-box partitioner in one process -- the call is split over every
+                                   device of the context (vector_add by element ranges on 16-byte
+                                   boundaries, matmul by 128-row blocks of A and C, B and the bias to
+                                   every device), each on the context's own stream (exec->stream NULL,
+                                   exec->device -1); returns when all devices are done (bounded by
+                                   timeout_ms each).  A split st_launch writes C in place. */
 
 typedef struct st_ctx st_ctx;
 

@@ -229,13 +229,14 @@ struct ExecCtx {
     int flags = 0;
 };
 
+constexpr const char *kAllDevicesScope =
+    "ST_EXEC_ALL_DEVICES applies to st_vector_add_host, st_matmul_host and st_launch with ST_EXEC_HOST_BUFFERS only";
+
 // `split_ok`: the call implements ST_EXEC_ALL_DEVICES (the host-memory
 // vector_add and matmul); every other entry point refuses the flag rather
 // than running on one device only.
 int resolve_exec(st_ctx *ctx, const st_exec *exec, ExecCtx *out, bool split_ok = false) {
-    if (exec && (exec->flags & ST_EXEC_ALL_DEVICES) && !split_ok)
-        return fail(ST_ERR_INVALID_ARGUMENT,
-                    "ST_EXEC_ALL_DEVICES applies to st_vector_add_host and st_matmul_host only");
+    if (exec && (exec->flags & ST_EXEC_ALL_DEVICES) && !split_ok) return fail(ST_ERR_INVALID_ARGUMENT, kAllDevicesScope);
     const int device = exec ? exec->device : -1;
     ST_TRY(get_dev(ctx, device, &out->dev));
     out->stream = (exec && exec->stream) ? static_cast<cudaStream_t>(exec->stream) : out->dev->stream;
@@ -820,6 +821,32 @@ int for_each_device_shard(st_ctx *ctx, const ExecCtx &x0, int64_t total, int64_t
     return rc;
 }
 
+// C = A + B on host memory over every device of the context: element
+// ranges on 16-byte boundaries for dense arrays, rows otherwise.
+int vector_add_host_split(st_ctx *ctx, const ExecCtx &x, const st_tensor &a, const st_tensor &b,
+                          const st_tensor &c) {
+    if (vector_add_host_flat(a, b, c)) {
+        int64_t n = 1;
+        for (int i = 0; i < c.rank; ++i) n *= c.shape[i];
+        return for_each_device_shard(ctx, x, n, 4, [&](const ExecCtx &xg, int64_t e0, int64_t e1) {
+            return vector_add_host_one(xg, flat_range(a, e0, e1), flat_range(b, e0, e1), flat_range(c, e0, e1),
+                                       false);
+        });
+    }
+    return for_each_device_shard(ctx, x, c.shape[0], 1, [&](const ExecCtx &xg, int64_t r0, int64_t r1) {
+        return vector_add_host_one(xg, host_rows(a, r0, r1), host_rows(b, r0, r1), host_rows(c, r0, r1), false);
+    });
+}
+
+// C = A @ B (+ bias) on host memory over every device of the context: 128-row
+// blocks of A and C per device, all of B and the bias to each.
+int matmul_host_split(st_ctx *ctx, const ExecCtx &x, const st_tensor &a, const st_tensor &b, const st_tensor *bias,
+                      const st_tensor &c) {
+    return for_each_device_shard(ctx, x, a.shape[0], 128, [&](const ExecCtx &xg, int64_t r0, int64_t r1) {
+        return matmul_host_one(xg, host_rows(a, r0, r1), b, bias, host_rows(c, r0, r1), false);
+    });
+}
+
 // ------------------------------------------------------------ entry registry
 enum class Kind { VectorAdd1D, VectorAdd2D, Matmul, Fma1D, Fma2D, Cast1D, Cast2D };
 
@@ -994,6 +1021,50 @@ int run_entry(const ExecCtx &x, const Entry &e, const st_grid &grid, std::vector
         return fail(ST_ERR_UNSUPPORTED, std::string(e.name) + ": the grid must cover all " + std::to_string(tiles) +
                                             " output tiles (the runtime picks its own tile shape)");
     return matmul_device(x, v[0], v[1], bias, v[2]);
+}
+
+// A host-buffer launch split over every device of the context
+// (ST_EXEC_ALL_DEVICES): the region the tile grid covers, by the same rules
+// as run_entry, goes to the split host calls, which write C in place.
+int run_entry_split(st_ctx *ctx, const ExecCtx &x, const Entry &e, const st_grid &grid, std::vector<st_tensor> &v,
+                    const int consts[3]) {
+    const int64_t blocks = static_cast<int64_t>(grid.x) * grid.y * grid.z;
+    if (e.kind == Kind::VectorAdd1D) {
+        for (int i = 0; i < 3; ++i)
+            if (v[i].dtype != ST_F32) return fail(ST_ERR_INVALID_ARGUMENT, "vector_add is f32-only");
+        const int64_t n = std::min<int64_t>(blocks * consts[0], v[2].shape[0]);
+        if (n > v[0].shape[0] || n > v[1].shape[0])
+            return fail(ST_ERR_INVALID_ARGUMENT, "vector_add: A and B must cover every stored element");
+        for (int i = 0; i < 3; ++i) v[i].shape[0] = n;
+        return vector_add_host_split(ctx, x, v[0], v[1], v[2]);
+    }
+    if (e.kind == Kind::VectorAdd2D) {
+        for (int i = 0; i < 3; ++i)
+            if (v[i].dtype != ST_F32) return fail(ST_ERR_INVALID_ARGUMENT, "vector_add_2d is f32-only");
+        int64_t rows = grid.z == 0 ? 0 : std::min<int64_t>(static_cast<int64_t>(grid.x) * consts[0], v[2].shape[0]);
+        const int64_t cols = std::min<int64_t>(static_cast<int64_t>(grid.y) * consts[1], v[2].shape[1]);
+        for (int i = 0; i < 2; ++i)
+            if (rows > v[i].shape[0] || cols > v[i].shape[1])
+                return fail(ST_ERR_INVALID_ARGUMENT, "vector_add_2d: A and B must cover every stored element");
+        for (int i = 0; i < 3; ++i) {
+            v[i].shape[0] = rows;
+            v[i].shape[1] = cols;
+        }
+        return vector_add_host_split(ctx, x, v[0], v[1], v[2]);
+    }
+    if (e.kind != Kind::Matmul)
+        return fail(ST_ERR_UNSUPPORTED, std::string(e.name) +
+                                            ": ST_EXEC_ALL_DEVICES splits vector_add, vector_add_2d and matmul entries");
+    const st_tensor *bias = e.bias ? &v[3] : nullptr;
+    ST_TRY(check_matmul(&v[0], &v[1], bias, &v[2]));
+    if (v[0].dtype != e.in_dtype)
+        return fail(ST_ERR_INVALID_ARGUMENT, std::string(e.name) + ": A/B dtype does not match the entry");
+    const int64_t tiles = cdiv(v[0].shape[0], consts[0]) * cdiv(v[1].shape[1], consts[1]);
+    if (blocks < 1) return fail(ST_ERR_INVALID_ARGUMENT, "empty grid");
+    if (!e.persistent && blocks < tiles)
+        return fail(ST_ERR_UNSUPPORTED, std::string(e.name) + ": the grid must cover all " + std::to_string(tiles) +
+                                            " output tiles (the runtime picks its own tile shape)");
+    return matmul_host_split(ctx, x, v[0], v[1], bias, v[2]);
 }
 
 }  // namespace
@@ -1180,12 +1251,19 @@ int st_launch(st_ctx *ctx, const char *entry_name, const st_grid *grid, const st
                                                   " was not found in the kernel registry.");
     if (!grid || (!params && n_params > 0) || n_params < 0)
         return fail(ST_ERR_INVALID_ARGUMENT, "grid and params are required");
+    const bool split = exec && (exec->flags & ST_EXEC_ALL_DEVICES);
+    if (split && !(exec->flags & ST_EXEC_HOST_BUFFERS))
+        return fail(ST_ERR_INVALID_ARGUMENT, kAllDevicesScope);
     ExecCtx x;
-    ST_TRY(resolve_exec(ctx, exec, &x));
+    ST_TRY(resolve_exec(ctx, exec, &x, true));
     std::vector<st_tensor> views;
     std::vector<int> bufpos;
     int consts[3];
     ST_TRY(parse_params(*e, params, n_params, &views, &bufpos, consts));
+    if (split) {  // host buffers split over every device: C is written in place
+        ST_TRY(check_all_devices(exec));
+        return run_entry_split(ctx, x, *e, *grid, views, consts);
+    }
     DeviceGuard guard(x.dev->ordinal);
     if (!(x.flags & ST_EXEC_HOST_BUFFERS)) {
         ST_TRY(run_entry(x, *e, *grid, views, consts));
@@ -1312,18 +1390,7 @@ int st_vector_add_host(st_ctx *ctx, const st_tensor *a, const st_tensor *b, cons
     ST_TRY(check_vector_add(a, b, c));
     if (x.flags & ST_EXEC_ALL_DEVICES) {
         ST_TRY(check_all_devices(exec));
-        if (vector_add_host_flat(*a, *b, *c)) {  // element ranges on 16-byte boundaries
-            int64_t n = 1;
-            for (int i = 0; i < c->rank; ++i) n *= c->shape[i];
-            return for_each_device_shard(ctx, x, n, 4, [&](const ExecCtx &xg, int64_t e0, int64_t e1) {
-                return vector_add_host_one(xg, flat_range(*a, e0, e1), flat_range(*b, e0, e1),
-                                           flat_range(*c, e0, e1), false);
-            });
-        }
-        return for_each_device_shard(ctx, x, c->shape[0], 1, [&](const ExecCtx &xg, int64_t r0, int64_t r1) {
-            return vector_add_host_one(xg, host_rows(*a, r0, r1), host_rows(*b, r0, r1), host_rows(*c, r0, r1),
-                                       false);
-        });
+        return vector_add_host_split(ctx, x, *a, *b, *c);
     }
     DeviceGuard guard(x.dev->ordinal);
     return vector_add_host_one(x, *a, *b, *c, true);
@@ -1336,10 +1403,7 @@ int st_matmul_host(st_ctx *ctx, const st_tensor *a, const st_tensor *b, const st
     ST_TRY(check_matmul(a, b, bias, c));
     if (x.flags & ST_EXEC_ALL_DEVICES) {
         ST_TRY(check_all_devices(exec));
-        // M-row blocks of 128: each device gets its rows of A and C, all of B and the bias
-        return for_each_device_shard(ctx, x, a->shape[0], 128, [&](const ExecCtx &xg, int64_t r0, int64_t r1) {
-            return matmul_host_one(xg, host_rows(*a, r0, r1), *b, bias, host_rows(*c, r0, r1), false);
-        });
+        return matmul_host_split(ctx, x, *a, *b, bias, *c);
     }
     DeviceGuard guard(x.dev->ordinal);
     return matmul_host_one(x, *a, *b, bias, *c, true);

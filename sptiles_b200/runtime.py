@@ -133,7 +133,8 @@ def grid_from_dispatch(entry_name: str, dispatch: Sequence[int], tile_elems: int
 def run_tile_kernel(*, entry_name: str | None = None, parameter_arrays: Iterable[np.ndarray],
                     output_indices: Iterable[int], dispatch: tuple[int, int, int] | None = None,
                     grid: tuple[int, int, int] | None = None, tile_elems: int | None = None, device: int = 0,
-                    timeout_ms: int = 60000, spirv_path=None, module=None) -> list[np.ndarray]:
+                    timeout_ms: int = 60000, spirv_path=None, module=None,
+                    devices: Sequence[int] | None = None) -> list[np.ndarray]:
     """Run a registered kernel on host arrays and return the output arrays.
 
     Same contract as run_spirv_kernel (spirv_runtime.py:153-174): every
@@ -150,6 +151,10 @@ def run_tile_kernel(*, entry_name: str | None = None, parameter_arrays: Iterable
     module) then names one of its entries, the bindings are checked against
     that entry's parameters, the module's tile sizes are the kernel
     constants, and ``tile_elems`` defaults to the module's tile.
+
+    ``devices`` splits the launch over those GPUs in this process
+    (ST_EXEC_ALL_DEVICES; vector_add and matmul entries): the region the
+    grid covers is divided by element ranges or 128-row blocks.
     """
     arrays = [np.ascontiguousarray(a) for a in parameter_arrays]
     outs = [int(i) for i in output_indices]
@@ -170,6 +175,10 @@ def run_tile_kernel(*, entry_name: str | None = None, parameter_arrays: Iterable
             params[i].bytes = a.nbytes
     out_idx = (ctypes.c_int32 * len(outs))(*outs)
     ex = N.StExec(None, device, N.ST_EXEC_HOST_BUFFERS | N.ST_EXEC_SYNC, timeout_ms, out_idx, len(outs))
+    ctx = context(device)
+    if devices is not None:
+        ex.device, ex.flags = -1, ex.flags | N.ST_EXEC_ALL_DEVICES
+        ctx = context_group(devices)
     if module is not None:
         from .module import TileModule
 
@@ -183,7 +192,7 @@ def run_tile_kernel(*, entry_name: str | None = None, parameter_arrays: Iterable
             if tile_elems is None or ent.backend_entry is None:
                 raise ValueError(f"entry {ent.name}: pass tile_elems or grid (the module does not fix its tile)")
             grid = grid_from_dispatch(ent.backend_entry, dispatch, tile_elems)
-        mod.launch(context(device), ent.name, grid, params, ex)
+        mod.launch(ctx, ent.name, grid, params, ex)
         return [arrays[i] for i in outs]
     if entry_name is None:
         raise ValueError("entry_name is required without a module")
@@ -194,7 +203,7 @@ def run_tile_kernel(*, entry_name: str | None = None, parameter_arrays: Iterable
             tile_elems = _default_tile_elems(entry_name)
         grid = grid_from_dispatch(entry_name, dispatch, tile_elems)
     g = N.StGrid(*[int(x) for x in grid])
-    N.check(N.lib().st_launch(context(device), entry_name.encode(), ctypes.byref(g), params, len(arrays),
+    N.check(N.lib().st_launch(ctx, entry_name.encode(), ctypes.byref(g), params, len(arrays),
                               ctypes.byref(ex)), f"st_launch({entry_name})")
     return [arrays[i] for i in outs]
 

@@ -109,3 +109,35 @@ def test_fused_allgather_between_devices_of_one_process():
     want = oracle.matmul_kat_expected(m, n, k).tobytes()
     for C in copies:
         assert C.cpu().numpy().tobytes() == want
+
+
+def test_host_buffer_launch_split_over_all_devices():
+    # run_spirv_kernel's contract (host arrays, a dispatch) with the launch split over every device
+    n = 1_000_003
+    rng = np.random.default_rng(8)
+    a = rng.uniform(-1, 1, n).astype(np.float32)
+    b = rng.uniform(-1, 1, n).astype(np.float32)
+    params = st.tensor_1d_descriptor(a) + st.tensor_1d_descriptor(b) + st.tensor_1d_descriptor(np.zeros(n, np.float32))
+    (c,) = st.run_tile_kernel(entry_name="vector_add", parameter_arrays=params, output_indices=[6],
+                              dispatch=(-(-n // 1024), 1, 1), devices=ALL)
+    assert c.tobytes() == (a + b).tobytes()
+    # a partial grid: only its tiles are computed, by whichever device holds them
+    params = st.tensor_1d_descriptor(a) + st.tensor_1d_descriptor(b) + \
+        st.tensor_1d_descriptor(np.full(n, -5.0, np.float32))
+    (c,) = st.run_tile_kernel(entry_name="vector_add", parameter_arrays=params, output_indices=[6], grid=(300, 1, 1),
+                              devices=ALL)
+    want = np.full(n, -5.0, np.float32)
+    oracle.vector_add_1d(a, b, want, 1024, 300)
+    assert c.tobytes() == want.tobytes()
+    # the reference's matmul_fp32 entry on its known answers
+    m, k, nn = 700, 333, 500
+    ka, kb = kat(m, nn, k)
+    params = st.tensor_2d_descriptor(ka) + st.tensor_2d_descriptor(kb) + \
+        st.tensor_2d_descriptor(np.zeros((m, nn), np.float32))
+    (c,) = st.run_tile_kernel(entry_name="matmul_fp32", parameter_arrays=params, output_indices=[10],
+                              grid=(-(-m // 32) * -(-nn // 32), 1, 1), devices=ALL)
+    assert c.reshape(m, nn).tobytes() == oracle.matmul_kat_expected(m, nn, k).tobytes()
+    # a matmul grid short of the tile count is refused, as on one device
+    with pytest.raises(NotImplementedError, match="must cover"):
+        st.run_tile_kernel(entry_name="matmul_fp32", parameter_arrays=params, output_indices=[10], grid=(3, 1, 1),
+                           devices=ALL)
