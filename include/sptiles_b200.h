@@ -282,9 +282,18 @@ int st_matmul_allgather(st_ctx *ctx, const st_tensor *a, const st_tensor *b, con
  * exec may be NULL; exec->stream NULL means the legacy default stream.
  *   - (M + N) * 3 * roundup(K, 32) * 4 bytes must fit in the array, else
  *     ST_ERR_INVALID_ARGUMENT; bias, if given, is f32.
- *   - The first call on a device finds the array's device address (set-up);
- *     make that first call before any stream capture.
- *   - All calls share the array: calls that overlap on the GPU race. */
+ *   - exec->stream, if given, must belong to the call's device.
+ *   - The first call on a device is its set-up: CUDA loads modules lazily,
+ *     so that call is when the array and the code of the kernels this entry
+ *     point launches take their device memory (it places them all at once,
+ *     and finds the array's device address).  Later calls allocate nothing.
+ *     A caller whose memory pool takes the GPU's memory makes one call per
+ *     device before that (any small product), and before any stream capture.
+ *   - All calls share the array: calls that overlap on the GPU race.
+ *   - A kernel that gives up a bounded wait leaves C incomplete and its code
+ *     in this entry point's abort word; the next call made with
+ *     ST_EXEC_SYNC returns ST_ERR_DEVICE_ABORT and clears the word (without
+ *     ST_EXEC_SYNC nothing is reported until then). */
 #define ST_STATIC_SCRATCH_BYTES (32u * 1024u * 1024u)
 int st_matmul_static_scratch(const st_tensor *a, const st_tensor *b, const st_tensor *bias, const st_tensor *c,
                              const st_exec *exec);

@@ -9,19 +9,28 @@
 // cudaMalloc; this entry point instead packs them into one fixed array that
 // is part of the library image, so a call allocates nothing.
 //
-// The array is a file-scope __device__ object: every GPU on which the
-// library is loaded holds its 32 MiB until the process exits.  Host code
-// cannot use the symbol `g_static_scratch` as a device address (on the host
-// it names a host-side stand-in), so the first call on each device, with
-// that device current, asks the runtime for the real address with
-// cudaGetSymbolAddress and keeps it.  Make that first call before any
-// stream capture.
+// The array is a file-scope __device__ object: once this file's module is
+// on a GPU, that GPU holds its 32 MiB until the process exits.  CUDA loads a
+// library's modules lazily by default (on first use), so the array, like
+// the code of the kernels this entry point launches, takes its device memory
+// during the first call on each device: that set-up call, made with the
+// device current, resolves the array's device address with
+// cudaGetSymbolAddress (host code cannot use the symbol `g_static_scratch`
+// as an address: on the host it names a host-side stand-in) and loads the
+// packing and GEMM kernels up front.  Later calls allocate nothing.  So a
+// caller whose memory pool takes the GPU's memory makes one call per device
+// before that (a 1 x 1 x 1 product will do), and, like every set-up, before
+// any stream capture.
 //
 // All calls share the one array, which keeps whatever the last call wrote.
 // The packing kernels overwrite every byte the GEMM then reads (padding
-// included), and the abort word is cleared at the start of each call.  Two
-// calls whose work overlaps on the GPU (different streams, or different host
-// threads) race on the array: serialise them.
+// included).  Two calls whose work overlaps on the GPU (different streams,
+// or different host threads) race on the array: serialise them.
+//
+// A kernel that gives up a bounded wait records a code in this file's abort
+// word and leaves C incomplete.  The word keeps that code until a call made
+// with ST_EXEC_SYNC reads it: that call returns ST_ERR_DEVICE_ABORT (for its
+// own work or for an earlier asynchronous call's) and clears the word.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -54,6 +63,20 @@ constexpr int kMaxDevices = 64;
 StaticDevice g_devices[kMaxDevices];
 std::mutex g_setup_mutex;
 
+// C = bias (or 0) when K == 0.
+__global__ void static_fill_kernel(void *c, int64_t ldc, int c_dtype, const void *bias, int bias_dtype, int64_t m,
+                                   int64_t n) {
+    const int64_t total = m * n;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t r = i / n, q = i - r * n;
+        const float v = bias ? static_cast<const float *>(bias)[q] : 0.0f;
+        if (c_dtype == ST_F32) static_cast<float *>(c)[r * ldc + q] = v;
+        else if (c_dtype == ST_F16) static_cast<__half *>(c)[r * ldc + q] = __float2half_rn(v);
+        else static_cast<__nv_bfloat16 *>(c)[r * ldc + q] = __float2bfloat16_rn(v);
+    }
+}
+
 // Once per device, with that device current: resolve the symbols' device addresses.
 int static_device(int dev, StaticDevice **out) {
     if (dev < 0 || dev >= kMaxDevices) return fail(ST_ERR_INVALID_ARGUMENT, "device ordinal out of range");
@@ -67,6 +90,11 @@ int static_device(int dev, StaticDevice **out) {
         void *scratch = nullptr, *word = nullptr;
         ST_CUDA_TRY(cudaGetSymbolAddress(&scratch, g_static_scratch));
         ST_CUDA_TRY(cudaGetSymbolAddress(&word, g_static_abort));
+        // the kernels later calls launch: their code is placed now, not on first launch
+        cudaFuncAttributes attr;
+        ST_CUDA_TRY(cudaFuncGetAttributes(&attr, static_fill_kernel));
+        ST_TRY(preload_pack_tf32_kernels());
+        ST_TRY(preload_gemm_tf32_kernels());
         d.scratch = static_cast<unsigned char *>(scratch);
         d.abort_word = static_cast<int *>(word);
         d.sm_count = sms;
@@ -86,20 +114,6 @@ int check_operand(const st_tensor *t, const char *name, int rank) {
     for (int i = 0; i < rank; ++i) empty |= t->shape[i] == 0;
     if (!empty && !t->data) return fail(ST_ERR_INVALID_ARGUMENT, std::string(name) + " has a null data pointer");
     return ST_OK;
-}
-
-// C = bias (or 0) when K == 0.
-__global__ void static_fill_kernel(void *c, int64_t ldc, int c_dtype, const void *bias, int bias_dtype, int64_t m,
-                                   int64_t n) {
-    const int64_t total = m * n;
-    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
-         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int64_t r = i / n, q = i - r * n;
-        const float v = bias ? static_cast<const float *>(bias)[q] : 0.0f;
-        if (c_dtype == ST_F32) static_cast<float *>(c)[r * ldc + q] = v;
-        else if (c_dtype == ST_F16) static_cast<__half *>(c)[r * ldc + q] = __float2half_rn(v);
-        else static_cast<__nv_bfloat16 *>(c)[r * ldc + q] = __float2bfloat16_rn(v);
-    }
 }
 
 // Bounded wait on the stream without creating any CUDA object.
@@ -155,23 +169,36 @@ extern "C" int st_matmul_static_scratch(const st_tensor *a, const st_tensor *b, 
         if (bias->shape[0] != N || bias->dtype != ST_F32 || (N > 1 && bias->strides[0] != 1))
             return fail(ST_ERR_INVALID_ARGUMENT, "bias must be a contiguous f32 vector of N elements");
     }
+    // (M + N) * 3 * kp * 4 bytes must fit; compared by division, so that no
+    // product of caller-supplied extents can wrap around
     const int64_t kp = tf32_packed_k(K);
-    const uint64_t need = static_cast<uint64_t>(M + N) * 3 * static_cast<uint64_t>(kp) * sizeof(float);
-    if (need > kStaticScratchBytes)
+    const uint64_t rows = static_cast<uint64_t>(M) + static_cast<uint64_t>(N);
+    const uint64_t row_bytes = 3 * static_cast<uint64_t>(kp) * sizeof(float);
+    if (row_bytes != 0 && rows > kStaticScratchBytes / row_bytes) {
+        const std::string need = rows <= UINT64_MAX / row_bytes ? std::to_string(rows * row_bytes) + " bytes"
+                                                                 : "more than 2^64 bytes";
         return fail(ST_ERR_INVALID_ARGUMENT,
-                    "st_matmul_static_scratch: this problem needs " + std::to_string(need) +
-                        " bytes of packed operands, the static scratch holds " +
-                        std::to_string(kStaticScratchBytes) + " bytes ((M + N) * 3 * roundup(K, 32) * 4 must fit)");
+                    "st_matmul_static_scratch: this problem needs " + need +
+                        " of packed operands, the static scratch holds " + std::to_string(kStaticScratchBytes) +
+                        " bytes ((M + N) * 3 * roundup(K, 32) * 4 must fit)");
+    }
     int dev = 0;
     if (exec && exec->device >= 0) dev = exec->device;
     else ST_CUDA_TRY(cudaGetDevice(&dev));
+    // NULL names the legacy default stream here: this entry point has no context
+    cudaStream_t stream = exec ? static_cast<cudaStream_t>(exec->stream) : nullptr;
+    if (stream != nullptr && stream != cudaStreamLegacy && stream != cudaStreamPerThread) {
+        int stream_dev = -1;
+        ST_CUDA_TRY(cudaStreamGetDevice(stream, &stream_dev));
+        if (stream_dev != dev)
+            return fail(ST_ERR_INVALID_ARGUMENT, "st_matmul_static_scratch: exec->stream belongs to device " +
+                                                     std::to_string(stream_dev) + ", the call runs on device " +
+                                                     std::to_string(dev));
+    }
     CurrentDevice guard(dev);
     StaticDevice *sd = nullptr;
     ST_TRY(static_device(dev, &sd));
-    // NULL names the legacy default stream here: this entry point has no context
-    cudaStream_t stream = exec ? static_cast<cudaStream_t>(exec->stream) : nullptr;
     if (M == 0 || N == 0) return ST_OK;
-    ST_CUDA_TRY(cudaMemsetAsync(sd->abort_word, 0, sizeof(int), stream));
     if (K == 0) {
         static_fill_kernel<<<148, 256, 0, stream>>>(c->data, c->strides[0], c->dtype, bias ? bias->data : nullptr,
                                                     ST_F32, M, N);
@@ -204,10 +231,13 @@ extern "C" int st_matmul_static_scratch(const st_tensor *a, const st_tensor *b, 
     }
     if (exec && (exec->flags & ST_EXEC_SYNC)) {
         ST_TRY(wait_stream(stream, exec->timeout_ms));
+        // this call's code, or one an earlier asynchronous call left behind
         int code = 0;
         ST_CUDA_TRY(cudaMemcpy(&code, sd->abort_word, sizeof(int), cudaMemcpyDeviceToHost));
-        if (code != 0)
+        if (code != 0) {
+            ST_CUDA_TRY(cudaMemset(sd->abort_word, 0, sizeof(int)));
             return fail(ST_ERR_DEVICE_ABORT, "a kernel gave up a bounded wait (code " + std::to_string(code) + ")");
+        }
     }
     return ST_OK;
 }

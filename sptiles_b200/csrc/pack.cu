@@ -243,6 +243,13 @@ int grid_1d(int64_t items) {
 
 int64_t tf32_packed_k(int64_t k) { return cdiv(k, 32) * 32; }
 
+int preload_pack_tf32_kernels() {
+    cudaFuncAttributes attr;
+    ST_CUDA_TRY(cudaFuncGetAttributes(&attr, pack_a_kernel));
+    ST_CUDA_TRY(cudaFuncGetAttributes(&attr, pack_b_kernel));
+    return ST_OK;
+}
+
 int launch_pack_a_tf32(const float *a, int64_t sa0, int64_t sa1, int64_t m, int64_t k, float *ap, int64_t kp,
                        cudaStream_t stream) {
     if (m <= 0 || kp <= 0) return ST_OK;
