@@ -123,7 +123,9 @@ struct GemmPlan {
     int tiles = 0;
 };
 
-int plan_gemm(int in_dtype, int64_t m, int64_t n, int64_t k, int sm_count, GemmPlan *plan);
+// sk_mode: the stream-K mode to score a partial last wave with (-1: the
+// environment's, else 1)
+int plan_gemm(int in_dtype, int64_t m, int64_t n, int64_t k, int sm_count, GemmPlan *plan, int sk_mode = -1);
 
 // D = A' B'^T-style tensor-core GEMM on operands already laid out for TMA:
 //   A: [M, K] row-major (K contiguous) of `ab_dtype` (ST_F16 / ST_BF16, or
@@ -157,8 +159,8 @@ struct GemmArgs {
     // stream_k_workspace_bytes, flags zero when idle
     float *sk_ws = nullptr;
     int *sk_flags = nullptr;
-    // C already holds 0 + bias (the pack kernel preset it): an L2-add
-    // stream-K launch then skips its own preset
+    // C already holds 0 + bias everywhere (the pack kernel preset it): an
+    // L2-add stream-K launch then skips its own preset of the split tiles
     bool c_preset = false;
     // fold split tiles in a fixed order (ST_EXEC_DETERMINISTIC)
     bool deterministic = false;
@@ -189,6 +191,12 @@ int launch_pack_a_tf32(const float *a, int64_t sa0, int64_t sa1, int64_t m, int6
                        cudaStream_t stream);
 int launch_pack_b_tf32(const float *b, int64_t sb0, int64_t sb1, int64_t k, int64_t n, float *bp, int64_t kp,
                        cudaStream_t stream);
+// CUDA places a kernel's code on the device at its first launch (lazy
+// loading); these place the 3xTF32 path's packing and GEMM kernels on the
+// current device now, for a caller that must make every device allocation
+// of the library up front.
+int preload_pack_tf32_kernels();
+int preload_gemm_tf32_kernels();
 // C[r, q] = 0 + bias[q] (or 0) for r < m, q < n, fp32, rows 16-byte aligned:
 // the starting value of an L2-add stream-K launch (c == nullptr: nothing)
 struct CPreset {

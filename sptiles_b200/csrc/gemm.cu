@@ -38,6 +38,8 @@
 
 namespace st {
 
+int launch_c_init_f32(const GemmArgs &g, int sm_count, cudaStream_t stream);
+
 // Tile raster of the cuTile matmul (matmul.py:14-24), shared by host and device.
 __host__ __device__ __forceinline__ void tile_raster(int64_t num_m, int64_t num_n, int64_t group_m, int64_t bid,
                                                      int64_t &bm, int64_t &bn) {
@@ -91,6 +93,7 @@ struct KParams {
     int sk_mode;     // stream_k_split mode
     int *sk_flags;   // per (pair, CTA, epilogue warp): partials stored and not yet folded
     int sk_l2add;    // 1: split units TMA-reduce-add their fp32 partials into C, which holds the bias
+    int k_snake;     // 1: a CTA's (pair's) odd-numbered whole tiles load their K blocks last to first
     void *c;
     void *c_peers[kMaxPeers];  // the same rows of C in other GPUs' copies (may be empty)
     int n_peers;
@@ -358,6 +361,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tile_raster(p.num_m_tiles, p.num_n_tiles, kGroupM, t, tm, tn);
                 const int m0 = static_cast<int>(tm) * kBlockM;
                 const int n0 = static_cast<int>(tn) * BN;
+                // k_snake: this CTA's odd-numbered tiles load K last to first, so a
+                // tile starts on the K blocks its predecessor read last, while they
+                // are still in L2 (the MMA only counts blocks; the sum order changes)
+                const bool rev = p.k_snake && ((t - static_cast<int>(blockIdx.x)) / static_cast<int>(gridDim.x)) & 1;
                 for (int kb = 0; kb < p.num_k_blocks; ++kb) {
                     if (!mbar_wait(empty_bar(s), ph ^ 1u, abort_flag, p.timeout_ns)) {
                         ok = false;
@@ -366,14 +373,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                     pending &= ~(1u << s);
                     const uint32_t sa = smem_addr(smem + s * Cfg::kStageBytes);
                     const uint32_t sb = sa + Cfg::kABytes;
+                    const int kx = (rev ? p.num_k_blocks - 1 - kb : kb) * kBK;
                     mbar_arrive_expect_tx(full_bar(s), Cfg::kStageBytes);
-                    tma_load_2d(sa, &tmap_a, full_bar(s), kb * kBK, m0, pol_a);
+                    tma_load_2d(sa, &tmap_a, full_bar(s), kx, m0, pol_a);
                     if constexpr (B_MN) {
 #pragma unroll
                         for (int j = 0; j < BN / 64; ++j)
-                            tma_load_2d(sb + j * (kBK * 128), &tmap_b, full_bar(s), n0 + 64 * j, kb * kBK, pol_b);
+                            tma_load_2d(sb + j * (kBK * 128), &tmap_b, full_bar(s), n0 + 64 * j, kx, pol_b);
                     } else {
-                        tma_load_2d(sb, &tmap_b, full_bar(s), kb * kBK, n0, pol_b);
+                        tma_load_2d(sb, &tmap_b, full_bar(s), kx, n0, pol_b);
                     }
                     pending |= 1u << s;
                     pending_ph = (pending_ph & ~(1u << s)) | (ph << s);
@@ -931,6 +939,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 tile_raster(num_m_pairs, num_n_pairs, kGroupM, w.tile, tm, tn);
                 const int m0 = static_cast<int>(tm) * 2 * kBlockM + static_cast<int>(rank) * kBlockM;
                 const int n0 = static_cast<int>(tn) * kPairN + static_cast<int>(rank) * kPairHalfN;
+                // k_snake: the pair's odd-numbered whole tiles load K last to first
+                // (stream-K units keep ascending K: their pairs sweep K together)
+                const bool rev = p.k_snake && w.tile < sched.dp_tiles && ((w.tile - pair) / num_pairs) & 1;
                 for (int kb = w.k0; kb < w.k1; ++kb) {
                     if (!mbar_wait(empty_bar(s), ph ^ 1u, abort_flag, p.timeout_ns)) {
                         ok = false;
@@ -943,13 +954,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     const uint32_t sa = smem_addr(smem + s * Cfg::kStageBytes);
                     const uint32_t sb = sa + Cfg::kABytes;
                     const uint32_t fb = even_full0 + 8u * s;
-                    tma_load_2d_pair(sa, &tmap_a, fb, kb * kBK, m0, pol_a);
+                    const int kx = (rev ? w.k0 + w.k1 - 1 - kb : kb) * kBK;
+                    tma_load_2d_pair(sa, &tmap_a, fb, kx, m0, pol_a);
                     if constexpr (B_MN) {
 #pragma unroll
                         for (int j = 0; j < kPairHalfN / 64; ++j)
-                            tma_load_2d_pair(sb + j * (kBK * 128), &tmap_b, fb, n0 + 64 * j, kb * kBK, pol_b);
+                            tma_load_2d_pair(sb + j * (kBK * 128), &tmap_b, fb, n0 + 64 * j, kx, pol_b);
                     } else {
-                        tma_load_2d_pair(sb, &tmap_b, fb, kb * kBK, n0, pol_b);
+                        tma_load_2d_pair(sb, &tmap_b, fb, kx, n0, pol_b);
                     }
                     if (++s == Cfg::kStages) {
                         s = 0;
@@ -1531,9 +1543,69 @@ int dispatch_bn(int bn, const CUtensorMap &ma, const CUtensorMap &mb, const KPar
     }
 }
 
+// C = 0 + bias (0 without a bias) on tiles [first, total) of the CTA-pair
+// raster only: the split tiles of an L2-add launch whose whole-tile waves
+// store their tiles outright.  Block b covers rows [32 (b % 8), +32) of
+// split tile b / 8; C's rows start 16-byte aligned (the staged-C rule).
+__global__ void __launch_bounds__(256) c_init_tiles_f32_kernel(float *c, long long ldc, const void *bias,
+                                                               int bias_dtype, int m, int n, int num_m_pairs,
+                                                               int num_n_pairs, int first, int total) {
+    pdl_wait();
+    const int blocks = (total - first) * 8;
+    for (int b = blockIdx.x; b < blocks; b += gridDim.x) {
+        int64_t tm, tn;
+        tile_raster(num_m_pairs, num_n_pairs, kGroupM, first + b / 8, tm, tn);
+        const int r0 = static_cast<int>(tm) * 2 * kBlockM + (b % 8) * 32;
+        const int q0 = static_cast<int>(tn) * kPairN;
+        for (int i = threadIdx.x; i < 32 * (kPairN / 4); i += blockDim.x) {
+            const int r = r0 + i / (kPairN / 4), q = q0 + 4 * (i % (kPairN / 4));
+            if (r >= m) break;  // rows grow with i
+            if (q >= n) continue;
+            float *dst = c + static_cast<long long>(r) * ldc + q;
+            if (q + 4 <= n) {
+                float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                if (bias != nullptr) {
+                    v.x = 0.0f + load_bias(bias, bias_dtype, q);
+                    v.y = 0.0f + load_bias(bias, bias_dtype, q + 1);
+                    v.z = 0.0f + load_bias(bias, bias_dtype, q + 2);
+                    v.w = 0.0f + load_bias(bias, bias_dtype, q + 3);
+                }
+                *reinterpret_cast<float4 *>(dst) = v;
+            } else {
+                for (int j = 0; q + j < n; ++j) dst[j] = bias != nullptr ? 0.0f + load_bias(bias, bias_dtype, q + j) : 0.0f;
+            }
+        }
+    }
+    pdl_trigger();
+}
+
+// The preset an L2-add CTA-pair launch of `pairs` pairs needs: the split
+// the kernel will derive from that grid decides which tiles are split; all
+// of C when every tile is, only the tail tiles after whole-tile waves.
+int launch_c_preset_f32(const GemmArgs &g, const KParams &kp, int pairs, int sm_count, cudaStream_t stream) {
+    const int num_m_pairs = (kp.m + 2 * kBlockM - 1) / (2 * kBlockM);
+    const int num_n_pairs = (kp.n + kPairN - 1) / kPairN;
+    const int total = num_m_pairs * num_n_pairs;
+    int dp = 0, skp = 0;
+    long long ski = 0;
+    stream_k_split(total, pairs, kp.num_k_blocks, kp.sk_mode, dp, skp, ski);
+    if (skp == 0) return ST_OK;  // nothing split: every tile is stored whole
+    if (dp == 0) return launch_c_init_f32(g, sm_count, stream);
+    const int blocks = (total - dp) * 8;
+    const int grid = blocks < 8 * sm_count ? blocks : 8 * sm_count;
+    ST_CUDA_TRY(launch_kernel(c_init_tiles_f32_kernel, static_cast<unsigned>(grid), 256, 0, stream,
+                              static_cast<float *>(g.c), static_cast<long long>(g.ldc), g.bias, g.bias_dtype, kp.m,
+                              kp.n, num_m_pairs, num_n_pairs, dp, total));
+    note_launch();
+    const cudaError_t e = cudaPeekAtLastError();
+    return e == cudaSuccess ? ST_OK : cuda_fail(cudaGetLastError(), "c_init_tiles_f32_kernel launch");
+}
+
+// preset: for an L2-add launch whose C is not preset yet, the call whose
+// split tiles get C = 0 + bias first (on the pair count actually launched)
 template <int FMT, bool B_MN>
 int launch_pair(const CUtensorMap &ma, const CUtensorMap &mb, const KParams &kp, const CStoreMaps &cm,
-                int pairs_wanted, cudaStream_t stream) {
+                int pairs_wanted, const GemmArgs *preset, int sm_count, cudaStream_t stream) {
     auto kern = gemm_tc_pair_kernel<FMT, B_MN>;
     static uint64_t attr_set = 0;
     static int max_clusters[64] = {0};
@@ -1564,6 +1636,7 @@ int launch_pair(const CUtensorMap &ma, const CUtensorMap &mb, const KParams &kp,
         }
     }
     const int pairs = pairs_wanted < clusters ? pairs_wanted : clusters;
+    if (preset != nullptr) ST_TRY(launch_c_preset_f32(*preset, kp, pairs, sm_count, stream));
     if (std::getenv("SPTILES_B200_DEBUG"))
         std::fprintf(stderr, "[sptiles_b200] pair gemm: %d pairs (wanted %d, co-resident clusters %d), smem %d\n",
                      pairs, pairs_wanted, clusters, PairCfg::kSmemBytes);
@@ -1655,6 +1728,7 @@ int launch_gemm_3xtf32(const GemmArgs &g, int sm_count, int *dev_err, uint64_t t
     kp.sk_flags = nullptr;
     kp.sk_mode = 0;
     kp.sk_l2add = 0;
+    kp.k_snake = 0;
     kp.staged = 0;  // direct stores
     kp.n_peers = g.peers.n;
     for (int i = 0; i < kMaxPeers; ++i) kp.c_peers[i] = i < g.peers.n ? g.peers.base[i] : nullptr;
@@ -1669,14 +1743,21 @@ int launch_gemm_3xtf32(const GemmArgs &g, int sm_count, int *dev_err, uint64_t t
     return launch_x3_instance<false, 64>(ma, mb, kp, plan.ctas, stream);
 }
 
-// Stream-K mode of the CTA-pair kernel (stream_k_split): SPTILES_B200_STREAM_K
-// = 0 whole tiles only, 2 also partial last waves; 1 (default) only problems
-// with fewer tiles than pairs.
-int stream_k_mode() {
+// Stream-K mode of the CTA-pair kernel (stream_k_split) set by
+// SPTILES_B200_STREAM_K: 0 whole tiles only, 1 only problems with fewer
+// tiles than pairs, 2 also partial last waves; -1 when unset.
+int stream_k_env() {
     const char *v = std::getenv("SPTILES_B200_STREAM_K");
     if (v != nullptr && v[0] == '0') return 0;
+    if (v != nullptr && v[0] == '1') return 1;
     if (v != nullptr && v[0] == '2') return 2;
-    return 1;
+    return -1;
+}
+
+// The mode plan_gemm scores with when it knows nothing about C.
+int stream_k_mode() {
+    const int env = stream_k_env();
+    return env >= 0 ? env : 1;
 }
 
 // two slots per pair (a stream-K range covers at most two tiles), each with
@@ -1691,7 +1772,8 @@ size_t stream_k_workspace_bytes(int sm_count) {
     return stream_k_flag_offset(sm_count) + static_cast<size_t>(pairs) * 2 * 2 * kEpilogueWarps * sizeof(int);
 }
 
-int plan_gemm(int in_dtype, int64_t m, int64_t n, int64_t k, int sm_count, GemmPlan *plan) {
+int plan_gemm(int in_dtype, int64_t m, int64_t n, int64_t k, int sm_count, GemmPlan *plan, int sk_mode) {
+    if (sk_mode < 0) sk_mode = stream_k_mode();
     if (m <= 0 || n <= 0 || k <= 0) return fail(ST_ERR_INVALID_ARGUMENT, "matmul extents must be positive");
     if (sm_count <= 0) sm_count = 148;
     // SPTILES_B200_GEMM_KERNEL=pair|single pins the kernel family (tests use it
@@ -1732,7 +1814,7 @@ int plan_gemm(int in_dtype, int64_t m, int64_t n, int64_t k, int sm_count, GemmP
         int dp_tiles = 0, sk_pairs = 0;
         long long sk_iters = 0;
         if (tiles < (int64_t(1) << 30))
-            stream_k_split(static_cast<int>(tiles), pairs, kb, stream_k_mode(), dp_tiles, sk_pairs, sk_iters);
+            stream_k_split(static_cast<int>(tiles), pairs, kb, sk_mode, dp_tiles, sk_pairs, sk_iters);
         if (sk_pairs > 0) {
             // per pair: whole tiles, its tail range, ~6 K blocks of partial store / fold
             const double work = static_cast<double>(dp_tiles / pairs) * kb +
@@ -1760,8 +1842,8 @@ int plan_gemm(int in_dtype, int64_t m, int64_t n, int64_t k, int sm_count, GemmP
         int pairs = best.tiles < sm_count / 2 ? best.tiles : sm_count / 2;
         int dp_tiles = 0, sk_pairs = 0;
         long long sk_iters = 0;
-        stream_k_split(best.tiles, sm_count / 2, static_cast<int>(cdiv(k, best.block_k)), stream_k_mode(),
-                       dp_tiles, sk_pairs, sk_iters);
+        stream_k_split(best.tiles, sm_count / 2, static_cast<int>(cdiv(k, best.block_k)), sk_mode, dp_tiles,
+                       sk_pairs, sk_iters);
         if (sk_pairs > 0) pairs = dp_tiles > 0 ? sm_count / 2 : sk_pairs;
         best.ctas = 2 * pairs;
     } else {
@@ -1791,28 +1873,43 @@ bool c_store_staged(const GemmArgs &g) {
     return ST_C_STORE_DEFAULT != 0;
 }
 
+// Whether split tiles of a CTA-pair launch can fold by L2 reduce-add: C is
+// fp32, staged and on this GPU only, and the caller accepts sums whose last
+// bit depends on the order in which L2 applies the units' adds (not
+// ST_EXEC_DETERMINISTIC, not SPTILES_B200_SK_FOLD=exchange).
+bool stream_k_l2add_ok(const GemmArgs &g) {
+    const char *v = std::getenv("SPTILES_B200_SK_FOLD");
+    const bool exchange = v != nullptr && std::strcmp(v, "exchange") == 0;
+    return !exchange && !g.deterministic && g.c_dtype == ST_F32 && g.peers.n == 0 && c_store_staged(g);
+}
+
+// Stream-K mode of one launch: SPTILES_B200_STREAM_K when set; otherwise 2
+// (a partial last wave after whole-tile waves is split too) where split
+// tiles fold by L2 reduce-add -- the tail then costs a preset of its tiles
+// and one reduce-add per unit -- and 1 where they would fold by exchange,
+// which on a tail measured slower than leaving the last wave partial.
+int stream_k_mode_for(const GemmArgs &g) {
+    const int env = stream_k_env();
+    if (env >= 0) return env;
+    return stream_k_l2add_ok(g) ? 2 : 1;
+}
+
 // How a CTA-pair launch folds the tiles a stream-K schedule splits:
-// kFoldL2Add where every tile is split and C is fp32, staged and on this GPU
-// only (units add their partials onto C preset to the bias);
-// kFoldExchange otherwise (reduce-scatter through the stream-K workspace,
-// whose sums come out the same bit for bit on every run; callers that ask
-// for that pass ST_EXEC_DETERMINISTIC, and SPTILES_B200_SK_FOLD=exchange
-// selects it everywhere).
+// kFoldL2Add where stream_k_l2add_ok (units add their partials onto C,
+// preset to the bias on the split tiles); kFoldExchange otherwise
+// (reduce-scatter through the stream-K workspace, whose sums come out the
+// same bit for bit on every run).
 int stream_k_fold(const GemmArgs &g, int sm_count) {
-    const int mode = stream_k_mode();
+    const int mode = stream_k_mode_for(g);
     if (mode <= 0) return kFoldNone;
     GemmPlan plan;
-    if (plan_gemm(g.ab_dtype, g.m, g.n, g.k, sm_count, &plan) != ST_OK || !plan.pair) return kFoldNone;
+    if (plan_gemm(g.ab_dtype, g.m, g.n, g.k, sm_count, &plan, mode) != ST_OK || !plan.pair) return kFoldNone;
     if (sm_count <= 0) sm_count = 148;
     int dp = 0, skp = 0;
     long long ski = 0;
     stream_k_split(plan.tiles, sm_count / 2, static_cast<int>(cdiv(g.k, plan.block_k)), mode, dp, skp, ski);
     if (skp == 0) return kFoldNone;
-    const char *v = std::getenv("SPTILES_B200_SK_FOLD");
-    const bool exchange = v != nullptr && std::strcmp(v, "exchange") == 0;
-    if (!exchange && !g.deterministic && dp == 0 && g.c_dtype == ST_F32 && g.peers.n == 0 && c_store_staged(g))
-        return kFoldL2Add;
-    return kFoldExchange;
+    return stream_k_l2add_ok(g) ? kFoldL2Add : kFoldExchange;
 }
 
 // Whether launch_gemm folds split tiles through the stream-K workspace (the
@@ -1856,10 +1953,28 @@ int launch_c_init_f32(const GemmArgs &g, int sm_count, cudaStream_t stream) {
     return e == cudaSuccess ? ST_OK : cuda_fail(cudaGetLastError(), "c_init_f32_kernel launch");
 }
 
+int preload_gemm_tf32_kernels() {
+    cudaFuncAttributes attr;
+    ST_CUDA_TRY(cudaFuncGetAttributes(&attr, gemm_tc_pair_kernel<2, false>));
+    ST_CUDA_TRY(cudaFuncGetAttributes(&attr, gemm_tc_kernel<2, false, 256>));
+    ST_CUDA_TRY(cudaFuncGetAttributes(&attr, gemm_tc_kernel<2, false, 128>));
+    ST_CUDA_TRY(cudaFuncGetAttributes(&attr, gemm_tc_kernel<2, false, 64>));
+    ST_CUDA_TRY(cudaFuncGetAttributes(&attr, c_init_f32_kernel));
+    ST_CUDA_TRY(cudaFuncGetAttributes(&attr, c_init_tiles_f32_kernel));
+    return ST_OK;
+}
+
+// SPTILES_B200_K_SNAKE=0 keeps every tile's K order ascending.
+bool k_snake_enabled() {
+    const char *v = std::getenv("SPTILES_B200_K_SNAKE");
+    return !(v != nullptr && v[0] == '0');
+}
+
 int launch_gemm(const GemmArgs &g, int sm_count, int *dev_err, uint64_t timeout_ns, cudaStream_t stream) {
     GemmPlan plan;
     // the packed tf32 K already includes the 3x expansion; plan on the product extents
-    ST_TRY(plan_gemm(g.ab_dtype, g.m, g.n, g.k, sm_count, &plan));
+    const int sk_mode = stream_k_mode_for(g);
+    ST_TRY(plan_gemm(g.ab_dtype, g.m, g.n, g.k, sm_count, &plan, sk_mode));
     const bool tf32 = g.ab_dtype == ST_F32;
     const int elem = tf32 ? 4 : 2;
     const int bk = kRowBytes / elem;
@@ -1900,8 +2015,9 @@ int launch_gemm(const GemmArgs &g, int sm_count, int *dev_err, uint64_t timeout_
     kp.err = dev_err;
     kp.timeout_ns = timeout_ns;
     const int fold = plan.pair ? stream_k_fold(g, sm_count) : kFoldNone;
-    kp.sk_mode = stream_k_mode();
+    kp.sk_mode = sk_mode;
     kp.sk_l2add = fold == kFoldL2Add ? 1 : 0;
+    kp.k_snake = k_snake_enabled() ? 1 : 0;
     kp.sk_ws = fold == kFoldExchange ? g.sk_ws : nullptr;
     kp.sk_flags = kp.sk_ws ? g.sk_flags : nullptr;
     CStoreMaps cm;
@@ -1919,14 +2035,15 @@ int launch_gemm(const GemmArgs &g, int sm_count, int *dev_err, uint64_t timeout_
     }
     if (plan.pair) {
         const int pairs = plan.ctas / 2;
-        if (kp.sk_l2add && !g.c_preset) ST_TRY(launch_c_init_f32(g, sm_count > 0 ? sm_count : 148, stream));
+        const GemmArgs *preset = kp.sk_l2add && !g.c_preset ? &g : nullptr;
+        const int sms = sm_count > 0 ? sm_count : 148;
         if (g.ab_dtype == ST_F16)
-            return g.b_k_major ? launch_pair<0, false>(ma, mb, kp, cm, pairs, stream)
-                               : launch_pair<0, true>(ma, mb, kp, cm, pairs, stream);
+            return g.b_k_major ? launch_pair<0, false>(ma, mb, kp, cm, pairs, preset, sms, stream)
+                               : launch_pair<0, true>(ma, mb, kp, cm, pairs, preset, sms, stream);
         if (g.ab_dtype == ST_BF16)
-            return g.b_k_major ? launch_pair<1, false>(ma, mb, kp, cm, pairs, stream)
-                               : launch_pair<1, true>(ma, mb, kp, cm, pairs, stream);
-        return launch_pair<2, false>(ma, mb, kp, cm, pairs, stream);
+            return g.b_k_major ? launch_pair<1, false>(ma, mb, kp, cm, pairs, preset, sms, stream)
+                               : launch_pair<1, true>(ma, mb, kp, cm, pairs, preset, sms, stream);
+        return launch_pair<2, false>(ma, mb, kp, cm, pairs, preset, sms, stream);
     }
     if (g.ab_dtype == ST_F16) {
         return g.b_k_major ? dispatch_bn<0, false>(plan.block_n, ma, mb, kp, cm, plan.ctas, stream)

@@ -161,6 +161,48 @@ def test_config_fp16_8192_cube_sampled_rows():
         assert rel_err(C[r0:r1].cpu().numpy(), want) <= 1e-2 * 0.1  # far inside the 1e-2 bound
 
 
+def fp64_product(A, B, bias=None):
+    """C = A @ B (+ bias) in fp64 on the GPU from the same rounded inputs: every
+    row of a full-size result checked against it (the oracle's row samples
+    above pin the arithmetic; this covers the rest of C)."""
+    C = A.double() @ B.double()
+    if bias is not None:
+        C += bias.double()
+    return C
+
+
+def full_rel_err(C, ref):
+    return ((C.double() - ref).abs().max() / ref.abs().max()).item()
+
+
+def test_config_fp16_8192_cube_every_row():
+    m = n = k = 8192
+    A, B = normal((m, k), 0.1, 3, torch.float16), normal((k, n), 0.1, 30, torch.float16)
+    C = st.matmul(A, B, out_dtype=torch.float32)
+    ref = fp64_product(A, B)
+    assert torch.isfinite(C).all()
+    # fp32 accumulation of 8192 products: ~1e-6 of max |C|; the bound is 1e-2
+    assert full_rel_err(C, ref) <= 1e-4
+
+
+def test_config_bf16_bias_every_row():
+    m, n, k = 32768, 4096, 4096
+    A, B = normal((m, k), 0.05, 4, torch.bfloat16), normal((k, n), 0.05, 40, torch.bfloat16)
+    g = torch.Generator(device="cpu").manual_seed(41)
+    bias = ((torch.rand(n, generator=g) * 2 - 1).to(torch.bfloat16)).to(DEV)
+    ref = fp64_product(A, B, bias)
+    C32 = st.matmul(A, B, bias, out_dtype=torch.float32)
+    assert full_rel_err(C32, ref) <= 1e-4
+    del C32
+    Cbf = st.matmul(A, B, bias)  # C takes A's dtype (matmul.py:245)
+    assert Cbf.dtype == torch.bfloat16
+    assert full_rel_err(Cbf, ref) <= 1e-2
+    # elementwise: one bf16 rounding of a sum that is fp32-accurate, so every
+    # element is within one bf16 step (2^-8 relative) of the fp64 value
+    d = (Cbf.double() - ref).abs()
+    assert bool((d <= ref.abs() * 2.0 ** -8 + 1e-5 * ref.abs().max()).all())
+
+
 def test_config_bf16_bias_sampled_rows():
     m, n, k = 32768, 4096, 4096
     A, B = normal((m, k), 0.05, 4, torch.bfloat16), normal((k, n), 0.05, 40, torch.bfloat16)
@@ -478,6 +520,96 @@ def test_stream_k_l2add_fold_random_bias(monkeypatch, dtype, mnk):
     order_tol = 5e-5 if dtype == torch.float32 else 1e-5
     assert rel_err(C.cpu().numpy(), C0.cpu().numpy()) <= order_tol
     assert rel_err(Cx.cpu().numpy(), C0.cpu().numpy()) <= order_tol
+
+
+# Shapes with whole-tile waves and a partial last wave (tiles >= pairs, more
+# than 3 % of the pairs idle in the last wave).  With fp32 C the last wave's
+# tiles are split over every pair by default and their units add onto C
+# preset to the bias on those tiles only; the whole tiles are stored outright.
+# (1024, 8192, 8192) is one rank's share of the fp16 configuration on 8 GPUs.
+WAVE_TAIL_SHAPES = [(1024, 8192, 1024), (2048, 8192, 640), (1000, 8000, 700), (3000, 5000, 520),
+                    (1024, 8192, 8192)]
+
+
+@pytest.mark.parametrize("sk", ["default", "0"], ids=["wave_tail", "whole_tiles"])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16], ids=["f32", "f16", "bf16"])
+@pytest.mark.parametrize("mnk", WAVE_TAIL_SHAPES, ids=lambda s: "x".join(map(str, s)))
+def test_stream_k_wave_tail_known_answers(monkeypatch, sk, dtype, mnk):
+    m, n, k = mnk
+    if dtype == torch.float32 and k > 2048:
+        pytest.skip("fp32 packs 3 K copies: the 8192-deep case is covered by the 16-bit inputs")
+    monkeypatch.setenv("SPTILES_B200_GEMM_KERNEL", "pair")
+    if sk != "default":
+        monkeypatch.setenv("SPTILES_B200_STREAM_K", sk)
+    A, B = kat(m, n, k, dtype)
+    C = torch.full((m, n), float("nan"), device=DEV)
+    st.matmul(A, B, out=C)
+    assert C.cpu().numpy().tobytes() == oracle.matmul_kat_expected(m, n, k).tobytes()
+
+
+@pytest.mark.parametrize("mnk", WAVE_TAIL_SHAPES[:4], ids=lambda s: "x".join(map(str, s)))
+def test_stream_k_wave_tail_random_bias(monkeypatch, mnk):
+    """The tail split with a bias (C preset to the bias on the split tiles)
+    against whole tiles, the exchange fold and the oracle; 16-bit C keeps
+    whole tiles and must match too."""
+    monkeypatch.setenv("SPTILES_B200_GEMM_KERNEL", "pair")
+    m, n, k = mnk
+    A, B = normal((m, k), 0.5, 70, torch.float16), normal((k, n), 0.5, 71, torch.float16)
+    bias = normal((n,), 1.0, 72, torch.float32)
+    C = torch.full((m, n), float("nan"), device=DEV)
+    st.matmul(A, B, bias, out=C)
+    for rows in ((0, 64), (m - 64, m)):
+        want = oracle_mm(A, B, bias, rows=rows)
+        assert rel_err(C[rows[0]:rows[1]].cpu().numpy(), want) <= TOL[torch.float16]
+    ref = fp64_product(A, B, bias)
+    assert full_rel_err(C, ref) <= 1e-5
+    monkeypatch.setenv("SPTILES_B200_SK_FOLD", "exchange")
+    Cx = st.matmul(A, B, bias, out_dtype=torch.float32)  # exchange: mode 1, whole tiles here
+    monkeypatch.delenv("SPTILES_B200_SK_FOLD")
+    monkeypatch.setenv("SPTILES_B200_STREAM_K", "2")
+    monkeypatch.setenv("SPTILES_B200_SK_FOLD", "exchange")
+    C2x = st.matmul(A, B, bias, out_dtype=torch.float32)  # the tail split folded by exchange
+    for other in (Cx, C2x):
+        assert rel_err(C.cpu().numpy(), other.cpu().numpy()) <= 1e-5
+    Ch = st.matmul(A, B, bias, out_dtype=torch.float16)
+    assert full_rel_err(Ch, ref) <= 1e-2
+
+
+def test_stream_k_wave_tail_replays_from_a_cuda_graph(monkeypatch):
+    """The tail's preset kernel and the GEMM captured once and replayed."""
+    monkeypatch.setenv("SPTILES_B200_GEMM_KERNEL", "pair")
+    m, n, k = 1024, 8192, 1024
+    A, B = kat(m, n, k, torch.float16)
+    out = torch.zeros((m, n), device=DEV)
+    st.matmul(A, B, out=out)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        st.matmul(A, B, out=out)
+    want = oracle.matmul_kat_expected(m, n, k).tobytes()
+    for _ in range(3):
+        out.fill_(float("nan"))
+        g.replay()
+        torch.cuda.synchronize()
+        assert out.cpu().numpy().tobytes() == want
+
+
+@pytest.mark.parametrize("kernel", ["pair", "single"])
+def test_k_order_alternation_matches_ascending_order(monkeypatch, kernel):
+    """A CTA's odd-numbered tiles load K last to first (L2 reuse between
+    consecutive tiles); only the summation order changes."""
+    monkeypatch.setenv("SPTILES_B200_GEMM_KERNEL", kernel)
+    m, n, k = 2048, 4096, 2048  # several tiles per CTA in both kernel families
+    A, B = normal((m, k), 0.5, 60, torch.float16), normal((k, n), 0.5, 61, torch.float16)
+    C = st.matmul(A, B, out_dtype=torch.float32)
+    monkeypatch.setenv("SPTILES_B200_K_SNAKE", "0")
+    C0 = st.matmul(A, B, out_dtype=torch.float32)
+    assert rel_err(C.cpu().numpy(), C0.cpu().numpy()) <= 1e-5
+    assert full_rel_err(C, fp64_product(A, B)) <= 1e-5
+    Ak, Bk = kat(m, n, k, torch.float16)
+    monkeypatch.delenv("SPTILES_B200_K_SNAKE")
+    assert st.matmul(Ak, Bk, out_dtype=torch.float32).cpu().numpy().tobytes() == \
+        oracle.matmul_kat_expected(m, n, k).tobytes()
 
 
 @pytest.mark.parametrize("mnk", [(1024, 1024, 1024), (300, 520, 2000)], ids=lambda s: "x".join(map(str, s)))
