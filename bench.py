@@ -68,6 +68,9 @@ def parse_args():
                         "all-gather of the row blocks")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-sweep", action="store_true", help="vector_add_1d: skip the N = 2^20 .. 2^28 sweep")
+    p.add_argument("--sustain-steps", type=int, default=300,
+                   help="matmul: after the timed steps, this many more back to back, reported under "
+                        "'sustained' with their own clock record (0: skip)")
     p.add_argument("--timing", choices=["auto", "graph", "eager"], default="auto",
                    help="graph: replay the K timed steps from one CUDA graph (host launch overhead out of the "
                         "timed region); eager: launch every step from the host; auto: graph for the "
@@ -91,30 +94,43 @@ def measured_peaks():
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
 
 
-def profile_traffic(key: str):
-    """DRAM bytes per launch from the committed ncu summary, if one exists."""
+def _traffic_line(key: str):
+    """Fields of the summary line for `key`: key, bytes, read, write, note."""
     f = ROOT / "profiles" / "traffic_per_launch.txt"
     if not f.exists():
         return None
     for line in f.read_text().splitlines():
-        parts = line.split()
+        parts = line.split(None, 4)
         if len(parts) >= 2 and parts[0] == key:
-            try:
-                return float(parts[1])
-            except ValueError:
-                return None
+            return parts
     return None
+
+
+def profile_traffic(key: str):
+    """DRAM bytes (read + write) per launch from the committed ncu summary, if one exists."""
+    parts = _traffic_line(key)
+    if parts is None:
+        return None
+    try:
+        return float(parts[1])
+    except ValueError:
+        return None
+
+
+def profile_traffic_note(key: str):
+    parts = _traffic_line(key)
+    return parts[4].strip() if parts is not None and len(parts) > 4 else None
 
 
 # ------------------------------------------------------------------ clocks
 class ClockSampler:
-    """Samples SM clock and clock-event reasons through NVML while running."""
+    """Samples SM clock, power and clock-event reasons through NVML while running."""
 
     REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
                0x80: "hw_power_brake_slowdown", 0x2: "applications_clocks_setting"}
 
     def __init__(self, device_index: int, period_s: float = 0.002):
-        self.samples, self.reasons, self.max_mhz = [], 0, None
+        self.samples, self.power_w, self.reasons, self.max_mhz = [], [], 0, None
         self._stop = threading.Event()
         self._thread = None
         self.error = None
@@ -137,6 +153,7 @@ class ClockSampler:
             try:
                 self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
                 self.reasons |= int(get_reasons(self._h))
+                self.power_w.append(nv.nvmlDeviceGetPowerUsage(self._h) / 1000.0)
             except Exception as e:  # pragma: no cover
                 self.error = str(e)
                 return
@@ -153,13 +170,27 @@ class ClockSampler:
         if self._thread:
             self._thread.join()
 
-    def summary(self):
+    def summary(self, ms_per_launch=None):
+        """Median SM clock, the samples binned by 100 MHz, power, and (given the
+        device time of one launch) the SM cycles one launch takes at that clock."""
         if self._nv is None or not self.samples:
             return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": len(self.samples),
                     "note": self.error or "no samples"}
-        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
-                "reasons": [v for k, v in self.REASONS.items() if self.reasons & k], "samples": len(self.samples),
-                "source": "NVML during the timed region"}
+        bins = {}
+        for mhz in self.samples:
+            lo = int(mhz) // 100 * 100
+            key = f"{lo}-{lo + 99}"
+            bins[key] = bins.get(key, 0) + 1
+        med = statistics.median(self.samples)
+        out = {"sm_mhz": med, "sm_max_mhz": self.max_mhz, "sm_mhz_min": min(self.samples),
+               "reasons": [v for k, v in self.REASONS.items() if self.reasons & k], "samples": len(self.samples),
+               "sm_mhz_bins": dict(sorted(bins.items())),
+               "power_w_median": round(statistics.median(self.power_w), 1) if self.power_w else None,
+               "power_w_max": round(max(self.power_w), 1) if self.power_w else None,
+               "source": "NVML every 2 ms during the timed region"}
+        if ms_per_launch:
+            out["cycles_per_launch_at_median_mhz"] = int(ms_per_launch * 1e-3 * med * 1e6)
+        return out
 
 
 # ------------------------------------------------------------------ inputs
@@ -201,13 +232,16 @@ def flops_of(wl, rows):
 
 
 # ------------------------------------------------------------------ our arm
-def time_steps(fn, steps, warmup, stream, dist_on, graph=True):
+def time_steps(fn, steps, warmup, stream, dist_on, graph=True, stats=None):
     """Device time (ms) of `steps` calls of `fn` after `warmup` calls.
 
     With ``graph`` the timed calls are captured once into a CUDA graph and
     the timed region is one replay of it: every step is still one full call
     of the hot path, but the host's per-call launch overhead leaves the
     timed region (what a launch-bound inner loop does in production).
+    Without it, an event between steps also gives each step's own device
+    time, summarised into ``stats`` when given (first / last / min / median /
+    max ms), which shows the clock settling under the power cap.
     Returns (ms, launches issued by the library for the timed steps).
     """
     import torch
@@ -232,18 +266,27 @@ def time_steps(fn, steps, warmup, stream, dist_on, graph=True):
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
     stream = torch.cuda.current_stream()
+    marks = []
     if g is None:
         before = st.kernel_launches()
+        marks = [torch.cuda.Event(enable_timing=True) for _ in range(steps - 1)]
     start.record(stream)
     if g is not None:
         g.replay()
     else:
         for i in range(steps):
             fn(i)
+            if i < steps - 1:
+                marks[i].record(stream)
     end.record(stream)
     torch.cuda.synchronize()
     if g is None:
         launches = st.kernel_launches() - before
+        if stats is not None and steps > 1:
+            ev = [start, *marks, end]
+            per = [ev[i].elapsed_time(ev[i + 1]) for i in range(steps)]
+            stats.update({"first": round(per[0], 5), "last": round(per[-1], 5), "min": round(min(per), 5),
+                          "median": round(statistics.median(per), 5), "max": round(max(per), 5)})
     if dist_on:
         dist.barrier()
     del g
@@ -318,10 +361,23 @@ def run_matmul(wl, args, rank, world, local, dist_on, peaks):
         else:
             gather_row_shards(c, wl["m"], out=c_full)
 
+    step_stats = {}
     with ClockSampler(local) as clk:
         ms, launches = time_steps(step, args.steps, args.warmup, stream, dist_on,
-                                  graph=use_graph(args, wl) and not replicate)
+                                  graph=use_graph(args, wl) and not replicate, stats=step_stats)
     ms_max = max_over_ranks(ms, dist_on)
+    sustained = None
+    if getattr(args, "sustain_steps", 0) and not replicate:
+        # the same steps back to back for a few hundred ms: the clock the
+        # 1000 W cap settles at, beside the short timed region's burst figure
+        n_s = args.sustain_steps
+        sus_stats = {}
+        with ClockSampler(local) as sclk:
+            s_ms, _ = time_steps(step, n_s, 0, stream, dist_on, graph=False, stats=sus_stats)
+        s_max = max_over_ranks(s_ms, dist_on)
+        sustained = {"steps": n_s, "ms_per_step": round(s_max / n_s, 5),
+                     "value": round(sum_over_ranks(flops_of(wl, rows), dist_on) * n_s / (s_max / 1e3) / 1e12, 3),
+                     "step_ms": sus_stats, "clocks": sclk.summary(s_ms / n_s)}
     gather = None
     kernel_ms = ms  # this rank's device time of the GEMM launches alone
     if replicate:
@@ -361,7 +417,7 @@ def run_matmul(wl, args, rank, world, local, dist_on, peaks):
         peak = peaks["bf16_tflops"] / 2.0 / 3.0  # tf32 runs at half the 16-bit rate, 3 passes
         peak_sus = peak_sus / 2.0 / 3.0
     key = f"matmul_{wl['dtype']}_{wl['m']}x{wl['n']}x{wl['k']}"
-    traffic = profile_traffic(key)
+    traffic = profile_traffic(key) if world == 1 else None  # captured on the 1-GPU workload
     plan = st.matmul_plan({"f16": 1, "bf16": 2, "f32": 0}[wl["dtype"]], rows or 1, wl["n"], wl["k"])
     roof = {"bound": "tensor", "achieved": round(achieved, 2), "peak": round(peak, 1), "unit": "TFLOP/s",
             "frac": round(achieved / peak, 4),
@@ -373,14 +429,58 @@ def run_matmul(wl, args, rank, world, local, dist_on, peaks):
             # the timed steps run back to back into the 1000 W cap: the measured
             # sustained (seconds-long cuBLAS loop) peak, for comparison
             "peak_sustained": round(peak_sus, 1), "frac_sustained": round(achieved / peak_sus, 4)}
+    if traffic is not None:
+        roof["traffic_note"] = profile_traffic_note(key)
     out = dict(value=value, ms_per_step=ms_max / args.steps, roofline=roof, gpu_launches=int(launches),
-               clocks=clk.summary(), plan=plan, rows=rows, allgather=gather)
+               clocks=clk.summary(ms / args.steps), plan=plan, rows=rows, allgather=gather)
+    if step_stats:
+        out["step_ms"] = step_stats
+    if sustained:
+        out["sustained"] = sustained
     if rep is not None:
         rep.close()
     del bufs[1:]
     if not args.no_e2e:
         out["e2e"] = e2e_matmul(wl, args, a, b, bias, out_dt, rows, dist_on)
     return out
+
+
+def host_link_probe(dev, h2d_bytes, d2h_bytes, dist_on):
+    """Pinned-memory copy rates of this box's host link, measured with the
+    e2e step's own byte counts: H2D alone, D2H alone, and both at once on two
+    streams (what a pipelined step overlaps).  With N ranks all ranks copy at
+    once, as their e2e steps do.  Returns GB/s figures and the link-bound
+    time of one step: max(H2D, D2H) bytes at the concurrent rates."""
+    import torch
+    nb_in, nb_out = max(h2d_bytes, 1 << 20), max(d2h_bytes, 1 << 20)
+    h_in = torch.empty(nb_in, dtype=torch.uint8).pin_memory()
+    h_out = torch.empty(nb_out, dtype=torch.uint8).pin_memory()
+    d_in = torch.empty(nb_in, dtype=torch.uint8, device=dev)
+    d_out = torch.empty(nb_out, dtype=torch.uint8, device=dev)
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+
+    def timed(do_in, do_out, reps=3):
+        best = float("inf")
+        for _ in range(reps):
+            torch.cuda.synchronize(dev)
+            if dist_on:
+                import torch.distributed as dist
+                dist.barrier()
+            t0 = time.perf_counter()
+            if do_in:
+                with torch.cuda.stream(s_in):
+                    d_in.copy_(h_in, non_blocking=True)
+            if do_out:
+                with torch.cuda.stream(s_out):
+                    h_out.copy_(d_out, non_blocking=True)
+            torch.cuda.synchronize(dev)
+            best = min(best, time.perf_counter() - t0)
+        return best
+    t_in, t_out, t_both = timed(True, False), timed(False, True), timed(True, True)
+    bound_s = t_both if h2d_bytes and d2h_bytes else max(t_in * h2d_bytes / nb_in, t_out * d2h_bytes / nb_out)
+    return {"h2d_GBps": round(nb_in / t_in / 1e9, 1), "d2h_GBps": round(nb_out / t_out / 1e9, 1),
+            "both_GBps": round((nb_in + nb_out) / t_both / 1e9, 1), "ms_per_step": round(bound_s * 1e3, 3),
+            "how": "pinned copies of this step's H2D and D2H byte counts on two streams at once (best of 3)"}
 
 
 def e2e_matmul(wl, args, a, b, bias, out_dt, rows, dist_on):
@@ -421,8 +521,17 @@ def e2e_matmul(wl, args, a, b, bias, out_dt, rows, dist_on):
     how = ("partition.sharded_matmul_host on each rank: its rows of A and 1/N of B's rows H2D, B all-gathered "
            "over NCCL, GEMM, its rows of C D2H" if dist_on else
            "sptiles_b200.matmul on pinned host tensors (st_matmul_host): H2D, kernel, D2H")
-    return {"value": round(total_flops * steps / dt / 1e12, 3), "unit": "TFLOP/s", "h2d_bytes_per_step": int(h2d),
-            "d2h_bytes_per_step": int(d2h), "steps": steps, "how": how + " per step, host wall clock"}
+    value = total_flops * steps / dt / 1e12
+    # per rank: its rows of A and its 1/N of B's rows in, its rows of C out
+    world = torch.distributed.get_world_size() if dist_on else 1
+    rank_h2d = ha.numel() * ha.element_size() + hb.numel() * hb.element_size() // world
+    link = host_link_probe(a.device, rank_h2d, hc.numel() * hc.element_size(), dist_on)
+    bound_ms = max_over_ranks(link["ms_per_step"], dist_on)
+    link["value"] = round(total_flops / (bound_ms / 1e3) / 1e12, 3)
+    link["frac"] = round(value / link["value"], 4)
+    return {"value": round(value, 3), "unit": "TFLOP/s", "h2d_bytes_per_step": int(h2d),
+            "d2h_bytes_per_step": int(d2h), "steps": steps, "how": how + " per step, host wall clock",
+            "link_bound": link}
 
 
 def vector_add_sweep(dev, peaks, exps=(20, 22, 24, 26, 28)):
@@ -493,8 +602,10 @@ def run_vector_add(wl, args, rank, world, local, dist_on, peaks):
             "peak_note": "of measured copy bandwidth" if peaks["source"] == "measured" else "of fallback",
             "traffic": profile_traffic(key), "kernel": "vadd_vec4_kernel",
             "ms_per_launch": round(ms / args.steps, 5)}
+    if roof["traffic"] is not None:
+        roof["traffic_note"] = profile_traffic_note(key)
     out = dict(value=value, ms_per_step=ms_max / args.steps, roofline=roof, gpu_launches=int(launches),
-               clocks=clk.summary(), sets=sets, elements=n)
+               clocks=clk.summary(ms / args.steps), sets=sets, elements=n)
     if len(wl["shape"]) == 1 and world == 1 and not args.no_sweep:
         del bufs
         out["sweep_1d"] = vector_add_sweep(dev, peaks)
@@ -512,9 +623,64 @@ def run_vector_add(wl, args, rank, world, local, dist_on, peaks):
         for _ in range(steps):
             st.vector_add(ha, hb, out=hc)
         dt = max_over_ranks(time.perf_counter() - t0, dist_on)
-        out["e2e"] = {"value": round(total_bytes * steps / dt / 1e9, 2), "unit": "GB/s",
-                      "h2d_bytes_per_step": 8 * n, "d2h_bytes_per_step": 4 * n, "steps": steps,
-                      "how": "sptiles_b200.vector_add on pinned host tensors (st_vector_add_host), host wall clock"}
+        e2e_value = total_bytes * steps / dt / 1e9
+        link = host_link_probe(dev, 8 * n, 4 * n, dist_on)
+        bound_ms = max_over_ranks(link["ms_per_step"], dist_on)
+        link["value"] = round(total_bytes / (bound_ms / 1e3) / 1e9, 2)
+        link["frac"] = round(e2e_value / link["value"], 4)
+        out["e2e"] = {"value": round(e2e_value, 2), "unit": "GB/s",
+                      "h2d_bytes_per_step": int(sum_over_ranks(8 * n, dist_on)),
+                      "d2h_bytes_per_step": int(sum_over_ranks(4 * n, dist_on)), "steps": steps,
+                      "how": "sptiles_b200.vector_add on pinned host tensors (st_vector_add_host), host wall clock",
+                      "link_bound": link}
+    return out
+
+
+def extra_entry(name, wl, sub, sub_args, world, unit):
+    """One configuration's measurement as a key of the bench line."""
+    e = {"workload": name, "value": round(sub["value"], 3), "unit": unit, "steps": sub_args.steps,
+         "warmup": sub_args.warmup, "ms_per_step": round(sub["ms_per_step"], 5), "roofline": sub["roofline"],
+         "e2e": sub.get("e2e"), "gpu_launches": sub["gpu_launches"], "clocks": sub["clocks"],
+         "config": config_of(name, wl, world, sub_args.timing)}
+    for k in ("sweep_1d", "step_ms", "allgather"):
+        if sub.get(k):
+            e[k] = sub[k]
+    if wl["kind"] == "matmul":
+        e["config"]["tile"] = f"{sub['plan']['block_m']}x{sub['plan']['block_n']}x{sub['plan']['block_k']}"
+    return e
+
+
+def run_extras(args, rank, world, local, dist_on, peaks):
+    """The other configurations, each with its own roofline and clock record.
+
+    One GPU: vector_add 1D 2^20 (with the 2^20 .. 2^28 sweep), fp32 1024^3
+    (3xTF32) and bf16 32768x4096x4096 + bias.  N GPUs: the bf16 + bias
+    configuration M-row sharded with C replicated on every rank, by the GEMM
+    epilogue's stores into every rank's copy (fused) and, timed beside it, by
+    the GEMM followed by an NCCL all-gather.  Every rank runs the same steps."""
+    out = {}
+    if world == 1:
+        plan = [("vector_add_1d", dict(steps=max(args.steps, 2000), warmup=max(args.warmup, 10), timing="graph")),
+                ("matmul_fp32", dict(steps=max(args.steps, 500), warmup=max(args.warmup, 10), timing="graph")),
+                ("matmul_bf16", dict(steps=args.steps, warmup=args.warmup, timing="eager"))]
+    else:
+        plan = [("matmul_bf16", dict(steps=args.steps, warmup=args.warmup, timing="eager", replicate="fused",
+                                     no_e2e=True))]
+    for name, over in plan:
+        wl = WORKLOADS[name]
+        sub_args = argparse.Namespace(**{**vars(args), "sustain_steps": 0, **over})
+        if wl["kind"] == "matmul":
+            sub = run_matmul(wl, sub_args, rank, world, local, dist_on, peaks)
+            unit = "TFLOP/s"
+        else:
+            sub = run_vector_add(wl, sub_args, rank, world, local, dist_on, peaks)
+            unit = "GB/s"
+        key = name + ("_replicated" if over.get("replicate") else "")
+        out[key] = extra_entry(name, wl, sub, sub_args, world, unit)
+        if over.get("replicate"):
+            out[key]["config"]["replicate_output"] = over["replicate"]
+        import torch
+        torch.cuda.empty_cache()
     return out
 
 
@@ -689,18 +855,15 @@ def main():
             res = run_matmul(wl, args, rank, world, local, dist_on, peaks)
         else:
             res = run_vector_add(wl, args, rank, world, local, dist_on, peaks)
-        secondary = None
+        secondary, extras = None, None
         if args.workload == "matmul_f16" and not args.no_secondary:
             vw = WORKLOADS["vector_add_2d"]
             # a ~35 us step needs more steps for a timed region the clock sampler can see
             sub_args = argparse.Namespace(**{**vars(args), "steps": max(args.steps, 1000),
                                              "warmup": max(args.warmup, 10)})
             sub = run_vector_add(vw, sub_args, rank, world, local, dist_on, peaks)
-            secondary = {"workload": "vector_add_2d", "value": round(sub["value"], 1), "unit": "GB/s",
-                         "steps": sub_args.steps, "warmup": sub_args.warmup,
-                         "ms_per_step": round(sub["ms_per_step"], 5), "roofline": sub["roofline"],
-                         "e2e": sub.get("e2e"), "gpu_launches": sub["gpu_launches"], "clocks": sub["clocks"],
-                         "config": config_of("vector_add_2d", vw, world, args.timing)}
+            secondary = extra_entry("vector_add_2d", vw, sub, sub_args, world, "GB/s")
+            extras = run_extras(args, rank, world, local, dist_on, peaks)
         cpu = None
         if rank == 0 and world == 1 and not args.no_cpu_baseline:
             cpu = cpu_baseline(wl)
@@ -723,6 +886,12 @@ def main():
                     line["allgather"] = res.get("allgather")
             if secondary:
                 line["vecadd"] = secondary
+            if extras:
+                line["configs"] = extras
+            if res.get("step_ms"):
+                line["step_ms"] = res["step_ms"]
+            if res.get("sustained"):
+                line["sustained"] = res["sustained"]
             if res.get("sweep_1d"):
                 line["sweep_1d"] = res["sweep_1d"]
             print(json.dumps(line), flush=True)
