@@ -92,7 +92,11 @@ struct KParams {
     float *sk_ws;    // stream-K partials (CTA-pair kernel); null: whole tiles only
     int sk_mode;     // stream_k_split mode
     int *sk_flags;   // per (pair, CTA, epilogue warp): partials stored and not yet folded
-    int sk_l2add;    // 1: split units TMA-reduce-add their fp32 partials into C, which holds the bias
+    // split tiles of an fp32 C fold in L2: 1 every unit TMA-reduce-adds its
+    // partial onto C preset to the bias; 2 (ordered) a tile's first unit
+    // stores its partial plus the bias outright and raises its flags, the
+    // tile's other units add onto that once the flags are up (no preset)
+    int sk_l2add;
     int k_snake;     // 1: a CTA's (pair's) odd-numbered whole tiles load their K blocks last to first
     void *c;
     void *c_peers[kMaxPeers];  // the same rows of C in other GPUs' copies (may be empty)
@@ -576,11 +580,16 @@ __device__ __forceinline__ uint64_t operand_l2_policy_b() {
 // columns, adds them and stores those columns of C.  No unit waits before
 // every unit of its pair has published, and the grid never exceeds the
 // co-resident clusters, so the waits end.  Where every tile is split and C is
-// fp32 on this GPU only (sk_l2add), there is no exchange: C is preset to the
-// bias by c_init_f32_kernel and each unit adds its whole partial tile onto C
-// with TMA reduce-adds, which L2 performs (the order of the units' adds, and
-// so the last bit of a sum, can differ between runs).  Stream-K index
-// q = P - 1 - pair.
+// fp32 on this GPU only (sk_l2add), there is no exchange: each unit adds its
+// whole partial tile onto C with TMA reduce-adds, which L2 performs (the
+// order of the units' adds, and so the last bit of a sum, can differ between
+// runs).  With stream-K flags (ordered mode) a tile's first unit -- the one
+// holding its K block 0, always the first split unit of its pair, which
+// never waits -- stores its partial plus the bias outright and raises one
+// flag per (CTA, epilogue warp) by the number of other units; each other
+// unit's warp waits (bounded) for the flag of its own rows, takes one count
+// off it and adds.  Without flags C is preset to the bias on the split
+// tiles first.  Stream-K index q = P - 1 - pair.
 enum : int { kUnitWhole = 0, kUnitSplit = 1 };
 
 struct PairWork {
@@ -1100,6 +1109,43 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             if (!wait_full(idx)) {
                 ok = false;
                 break;
+            }
+            if (w.kind != kUnitWhole && p.sk_l2add == 2) {  // ordered L2 fold (see above)
+                const SplitTile t = split_tile(p, sched, w);
+                int *flag = sk_flag(p, sk_slot(sched, t.q0, t.rel), rank, g);
+                if (t.j == 0) {
+                    store_c(w, idx, 0, kPairN, false);
+                    if (lane == 0) {
+                        bulk_wait_group_all();  // this warp's rows of the tile are in C
+                        fence_proxy_async_global();
+                        red_release_gpu_add(flag, t.n - 1);
+                    }
+                    __syncwarp();
+                } else {
+                    bool up = true;
+                    if (lane == 0) {
+                        const uint64_t t0 = global_timer_ns();
+                        while (ld_acquire_gpu(flag) < 1) {
+                            if (*abort_flag != 0 || global_timer_ns() - t0 > p.timeout_ns) {
+                                up = false;
+                                break;
+                            }
+                        }
+                        if (up) {
+                            fence_proxy_async_global();  // the acquire comes before the reduce-adds
+                            atomicSub(flag, 1);
+                        }
+                    }
+                    if (!__shfl_sync(0xffffffffu, up, 0)) {
+                        *abort_flag = 1;
+                        if (lane == 0) atomicExch(p.err, kDevAbortGemmStreamK);
+                        ok = false;
+                        break;
+                    }
+                    store_c(w, idx, 0, kPairN, true);
+                }
+                release(idx);
+                continue;
             }
             if (w.kind == kUnitWhole || p.sk_l2add) {  // a split unit adds its partial onto C in L2
                 store_c(w, idx, 0, kPairN, w.kind != kUnitWhole);
@@ -1912,10 +1958,11 @@ int stream_k_fold(const GemmArgs &g, int sm_count) {
     return stream_k_l2add_ok(g) ? kFoldL2Add : kFoldExchange;
 }
 
-// Whether launch_gemm folds split tiles through the stream-K workspace (the
+// Whether launch_gemm uses the stream-K workspace: the exchange folds
+// through its partials and flags, the ordered L2 fold through its flags (the
 // workspace is only acquired then, so other calls put no event between
 // their launches).
-bool gemm_uses_stream_k(const GemmArgs &g, int sm_count) { return stream_k_fold(g, sm_count) == kFoldExchange; }
+bool gemm_uses_stream_k(const GemmArgs &g, int sm_count) { return stream_k_fold(g, sm_count) != kFoldNone; }
 
 // C[r, q] = 0 + bias[q] (0 without a bias) for r < m, q < n: the value the
 // split units of an L2-add stream-K launch add their partial tiles onto.
@@ -1962,6 +2009,12 @@ int preload_gemm_tf32_kernels() {
     ST_CUDA_TRY(cudaFuncGetAttributes(&attr, c_init_f32_kernel));
     ST_CUDA_TRY(cudaFuncGetAttributes(&attr, c_init_tiles_f32_kernel));
     return ST_OK;
+}
+
+// SPTILES_B200_SK_FOLD=preset: the L2 fold presets C even when flags exist.
+bool sk_ordered_enabled() {
+    const char *v = std::getenv("SPTILES_B200_SK_FOLD");
+    return !(v != nullptr && std::strcmp(v, "preset") == 0);
 }
 
 // SPTILES_B200_K_SNAKE=0 keeps every tile's K order ascending.
@@ -2016,10 +2069,11 @@ int launch_gemm(const GemmArgs &g, int sm_count, int *dev_err, uint64_t timeout_
     kp.timeout_ns = timeout_ns;
     const int fold = plan.pair ? stream_k_fold(g, sm_count) : kFoldNone;
     kp.sk_mode = sk_mode;
-    kp.sk_l2add = fold == kFoldL2Add ? 1 : 0;
+    // the ordered L2 fold needs the stream-K flags; without them C is preset
+    kp.sk_l2add = fold == kFoldL2Add ? (g.sk_flags != nullptr && sk_ordered_enabled() ? 2 : 1) : 0;
     kp.k_snake = k_snake_enabled() ? 1 : 0;
     kp.sk_ws = fold == kFoldExchange ? g.sk_ws : nullptr;
-    kp.sk_flags = kp.sk_ws ? g.sk_flags : nullptr;
+    kp.sk_flags = fold != kFoldNone ? g.sk_flags : nullptr;
     CStoreMaps cm;
     std::memset(&cm, 0, sizeof(cm));
     kp.staged = 0;
@@ -2035,7 +2089,7 @@ int launch_gemm(const GemmArgs &g, int sm_count, int *dev_err, uint64_t timeout_
     }
     if (plan.pair) {
         const int pairs = plan.ctas / 2;
-        const GemmArgs *preset = kp.sk_l2add && !g.c_preset ? &g : nullptr;
+        const GemmArgs *preset = kp.sk_l2add == 1 && !g.c_preset ? &g : nullptr;
         const int sms = sm_count > 0 ? sm_count : 148;
         if (g.ab_dtype == ST_F16)
             return g.b_k_major ? launch_pair<0, false>(ma, mb, kp, cm, pairs, preset, sms, stream)

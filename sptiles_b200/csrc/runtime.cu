@@ -411,9 +411,13 @@ int matmul_device(const ExecCtx &x, const st_tensor &a, const st_tensor &b, cons
         g.ldb = 3 * kp;
         g.b_k_major = true;
         g.k = 3 * kp;
-        // an L2-add stream-K launch starts from C = bias: the pack writes it
+        // split tiles fold through the stream-K workspace's flags; an L2-add
+        // launch without them (a capture before the workspace exists) starts
+        // from C = bias, which the pack writes
+        const int fold = stream_k_fold(g, x.dev->sm_count);
+        if (fold != kFoldNone) ST_TRY(sk_acquire(x.dev, x.stream, g));
         CPreset preset;
-        if (stream_k_fold(g, x.dev->sm_count) == kFoldL2Add) {
+        if (fold == kFoldL2Add && g.sk_flags == nullptr) {
             preset.c = static_cast<float *>(c.data);
             preset.ldc = c.strides[0];
             preset.bias = bias_ptr;
@@ -425,7 +429,6 @@ int matmul_device(const ExecCtx &x, const st_tensor &a, const st_tensor &b, cons
         ST_TRY(launch_pack_ab_tf32(static_cast<const float *>(a.data), a.strides[0], a.strides[1], M,
                                    static_cast<const float *>(b.data), b.strides[0], b.strides[1], N, K, ap, bp, kp,
                                    g.c_preset ? &preset : nullptr, x.stream));
-        if (gemm_uses_stream_k(g, x.dev->sm_count)) ST_TRY(sk_acquire(x.dev, x.stream, g));
         ST_TRY(launch_gemm(g, x.dev->sm_count, x.dev->dev_err, kDeviceWaitLimitNs, x.stream));
         if (g.sk_ws) ST_TRY(ws_release(x.dev->sk, x.stream));
         return ws_release(ws, x.stream);

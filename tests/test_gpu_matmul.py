@@ -498,13 +498,17 @@ def test_stream_k_exchange_fold_known_answers(monkeypatch, dtype, mnk):
     assert C.cpu().numpy().tobytes() == oracle.matmul_kat_expected(m, n, k).tobytes()
 
 
+@pytest.mark.parametrize("fold", ["ordered", "preset"])
 @pytest.mark.parametrize("dtype", [torch.float32, torch.float16], ids=["f32", "f16"])
 @pytest.mark.parametrize("mnk", [(1024, 1024, 1024), (300, 520, 2000), (1000, 3000, 2000)],
                          ids=lambda s: "x".join(map(str, s)))
-def test_stream_k_l2add_fold_random_bias(monkeypatch, dtype, mnk):
-    """Split tiles added onto C preset to the bias agree with whole tiles and
-    with the exchange up to summation order, and with the oracle."""
+def test_stream_k_l2add_fold_random_bias(monkeypatch, fold, dtype, mnk):
+    """Split tiles added in L2 (onto a first unit's store, or onto C preset to
+    the bias) agree with whole tiles and with the exchange up to summation
+    order, and with the oracle."""
     monkeypatch.setenv("SPTILES_B200_GEMM_KERNEL", "pair")
+    if fold == "preset":
+        monkeypatch.setenv("SPTILES_B200_SK_FOLD", "preset")
     m, n, k = mnk
     A, B = normal((m, k), 0.5, 90, dtype), normal((k, n), 0.5, 91, dtype)
     bias = normal((n,), 1.0, 92, torch.float32)
@@ -531,16 +535,21 @@ WAVE_TAIL_SHAPES = [(1024, 8192, 1024), (2048, 8192, 640), (1000, 8000, 700), (3
                     (1024, 8192, 8192)]
 
 
-@pytest.mark.parametrize("sk", ["default", "0"], ids=["wave_tail", "whole_tiles"])
+@pytest.mark.parametrize("sk", ["ordered", "preset", "whole"])
 @pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16], ids=["f32", "f16", "bf16"])
 @pytest.mark.parametrize("mnk", WAVE_TAIL_SHAPES, ids=lambda s: "x".join(map(str, s)))
 def test_stream_k_wave_tail_known_answers(monkeypatch, sk, dtype, mnk):
+    """ordered: a split tile's first unit stores, the others add after its
+    flags (the default); preset: C preset on the split tiles, every unit adds;
+    whole: no split."""
     m, n, k = mnk
     if dtype == torch.float32 and k > 2048:
         pytest.skip("fp32 packs 3 K copies: the 8192-deep case is covered by the 16-bit inputs")
     monkeypatch.setenv("SPTILES_B200_GEMM_KERNEL", "pair")
-    if sk != "default":
-        monkeypatch.setenv("SPTILES_B200_STREAM_K", sk)
+    if sk == "preset":
+        monkeypatch.setenv("SPTILES_B200_SK_FOLD", "preset")
+    elif sk == "whole":
+        monkeypatch.setenv("SPTILES_B200_STREAM_K", "1")
     A, B = kat(m, n, k, dtype)
     C = torch.full((m, n), float("nan"), device=DEV)
     st.matmul(A, B, out=C)
@@ -563,6 +572,10 @@ def test_stream_k_wave_tail_random_bias(monkeypatch, mnk):
         assert rel_err(C[rows[0]:rows[1]].cpu().numpy(), want) <= TOL[torch.float16]
     ref = fp64_product(A, B, bias)
     assert full_rel_err(C, ref) <= 1e-5
+    monkeypatch.setenv("SPTILES_B200_SK_FOLD", "preset")
+    Cp = torch.full((m, n), float("nan"), device=DEV)
+    st.matmul(A, B, bias, out=Cp)  # every unit adds onto C preset to the bias
+    assert rel_err(C.cpu().numpy(), Cp.cpu().numpy()) <= 1e-5
     monkeypatch.setenv("SPTILES_B200_SK_FOLD", "exchange")
     Cx = st.matmul(A, B, bias, out_dtype=torch.float32)  # exchange: mode 1, whole tiles here
     monkeypatch.delenv("SPTILES_B200_SK_FOLD")
