@@ -124,8 +124,9 @@ struct GemmPlan {
 };
 
 // sk_mode: the stream-K mode to score a partial last wave with (-1: the
-// environment's, else 1)
-int plan_gemm(int in_dtype, int64_t m, int64_t n, int64_t k, int sm_count, GemmPlan *plan, int sk_mode = -1);
+// environment's, else 1); force_pair: the CTA-pair plan whatever the scores
+int plan_gemm(int in_dtype, int64_t m, int64_t n, int64_t k, int sm_count, GemmPlan *plan, int sk_mode = -1,
+              bool force_pair = false);
 
 // D = A' B'^T-style tensor-core GEMM on operands already laid out for TMA:
 //   A: [M, K] row-major (K contiguous) of `ab_dtype` (ST_F16 / ST_BF16, or
@@ -164,7 +165,14 @@ struct GemmArgs {
     bool c_preset = false;
     // fold split tiles in a fixed order (ST_EXEC_DETERMINISTIC)
     bool deterministic = false;
+    // ab_dtype ST_F32 with raw fp32 A [M, K] and B (K-major [N, K] or
+    // N-contiguous [K, N]) and the true K: the CTA-pair kernel splits the
+    // tiles into tf32 hi / lo itself (3xTF32); only when gemm_split_fp32_fits
+    bool split_fp32 = false;
 };
+// Whether launch_gemm can take these fp32 operands raw (split_fp32): the
+// plan picks the CTA-pair kernel and TMA can address A and B in place.
+bool gemm_split_fp32_fits(const GemmArgs &args, int sm_count);
 // Partial accumulators (one 256 x 256 fp32 tile per CTA pair) and arrival
 // flags of the stream-K tail, for up to sm_count / 2 pairs.
 size_t stream_k_workspace_bytes(int sm_count);
@@ -174,6 +182,9 @@ bool gemm_uses_stream_k(const GemmArgs &args, int sm_count);
 // How launch_gemm folds the tiles a stream-K schedule splits.
 enum : int { kFoldNone = 0, kFoldExchange = 1, kFoldL2Add = 2 };
 int stream_k_fold(const GemmArgs &args, int sm_count);
+// For kFoldL2Add: 2 when split tiles fold ordered (needs the stream-K
+// flags), 1 when C must hold 0 + bias first; 0 for other folds.
+int stream_k_l2add_mode(const GemmArgs &args, int sm_count);
 size_t stream_k_flag_offset(int sm_count);
 int launch_gemm(const GemmArgs &args, int sm_count, int *dev_err, uint64_t timeout_ns, cudaStream_t stream);
 // fp32 A and B used in place (TMA-addressable): the split into tf32 hi/lo

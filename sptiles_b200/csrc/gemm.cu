@@ -32,6 +32,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <type_traits>
 
 #include "common.h"
 #include "sm100.cuh"
@@ -857,30 +858,75 @@ struct PairCfg {
     static constexpr int kBBytes = kPairHalfN * kRowBytes;
     static constexpr int kStageBytes = kABytes + kBBytes;
     static constexpr int kStages = ST_PAIR_STAGES;
+    static constexpr int kRawStages = 0;
+    static constexpr int kRawStageBytes = 0;
+    static constexpr int kRingBytes = kStages * kStageBytes;
+    static constexpr int kThreadCount = kThreads;
     static constexpr int kTmemCols = 512;  // two 256-column accumulators
-    static constexpr int kSmemBytes = kStages * kStageBytes + kBarRegion + kCStagingBytes + 1024;
+    static constexpr int kSmemBytes = kRingBytes + kBarRegion + kCStagingBytes + 1024;
     static_assert(kSmemBytes <= 232448, "over the per-block shared memory limit");
-    static_assert(kStages * kStageBytes >= kEpilogueWarps * kLandBoxes * kStageBoxBytes,
+    static_assert(kRingBytes >= kEpilogueWarps * kLandBoxes * kStageBoxBytes,
                   "the operand ring must hold every epilogue warp's stream-K landing slice");
 };
 
-template <int FMT, bool B_MN>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+// fp32 A and B split into tf32 inside the CTA-pair kernel (3xTF32): TMA
+// brings raw fp32 tiles (A: 128 rows x 32 K; B: 128 columns x 32 K, as K-major
+// rows or as four N-contiguous 32 x 32 boxes) into a raw ring; converter
+// warps write hi = x with its 13 low mantissa bits cleared and lo = (x - hi)
+// likewise cleared -- exact tf32 values, whatever the tensor core does with
+// dropped bits -- into the MMA ring, K-major (an N-contiguous B is transposed
+// on the way); the even CTA issues lo*hi, hi*lo and hi*hi per K step of 8.
+// x - hi is exact in fp32, so x = hi + lo up to 2^-20 |x|.
+#ifndef ST_X3_CONV_WARPS
+#define ST_X3_CONV_WARPS 8
+#endif
+constexpr int kX3ConvWarps = ST_X3_CONV_WARPS;
+struct X3PairCfg {
+    static constexpr int kABytes = kBlockM * kRowBytes;       // 128 rows x 32 fp32
+    static constexpr int kBBytes = kPairHalfN * kRowBytes;    // 128 columns x 32 fp32
+    static constexpr int kStageBytes = 2 * kABytes + 2 * kBBytes;  // A hi, A lo, B hi, B lo
+    static constexpr int kStages = 2;
+    static constexpr int kRawStageBytes = kABytes + kBBytes;  // raw A, raw B
+    static constexpr int kRawStages = 2;
+    static constexpr int kRingBytes = kStages * kStageBytes + kRawStages * kRawStageBytes;
+    static constexpr int kThreadCount = kThreads + 32 * kX3ConvWarps;
+    static constexpr int kTmemCols = 512;
+    static constexpr int kSmemBytes = kRingBytes + kBarRegion + kCStagingBytes + 1024;
+    static_assert(kSmemBytes <= 232448, "over the per-block shared memory limit");
+    static_assert(kRingBytes >= kEpilogueWarps * kLandBoxes * kStageBoxBytes,
+                  "the operand ring must hold every epilogue warp's stream-K landing slice");
+};
+
+// x with its 13 low mantissa bits cleared: exactly representable in tf32.
+__device__ __forceinline__ float tf32_trunc(float x) { return __uint_as_float(__float_as_uint(x) & 0xffffe000u); }
+
+// hi / lo of four values: hi = tf32_trunc(x), lo = tf32_trunc(x - hi).
+__device__ __forceinline__ void split4(const float4 &x, float4 &hi, float4 &lo) {
+    hi = make_float4(tf32_trunc(x.x), tf32_trunc(x.y), tf32_trunc(x.z), tf32_trunc(x.w));
+    lo = make_float4(tf32_trunc(x.x - hi.x), tf32_trunc(x.y - hi.y), tf32_trunc(x.z - hi.z), tf32_trunc(x.w - hi.w));
+}
+
+template <int FMT, bool B_MN, bool X3 = false>
+__global__ void __cluster_dims__(2, 1, 1)
+    __launch_bounds__(X3 ? X3PairCfg::kThreadCount : PairCfg::kThreadCount, 1)
     gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                         const KParams p, const __grid_constant__ CStoreMaps cmaps) {
-    using Cfg = PairCfg;
+    using Cfg = std::conditional_t<X3, X3PairCfg, PairCfg>;
     constexpr bool kTf32 = FMT == 2;
     constexpr int kElem = kTf32 ? 4 : 2;
     constexpr int kBK = kRowBytes / kElem;
     constexpr int kMmaK = 32 / kElem;
     constexpr int kKSteps = kBK / kMmaK;
-    constexpr uint32_t kIdesc = mma_idesc(FMT, false, B_MN, 2 * kBlockM, kPairN);
-    static_assert(!(kTf32 && B_MN), "tf32 operands are packed K-major");
+    // the split variant hands the tensor core K-major tiles whatever B's layout
+    constexpr uint32_t kIdesc = mma_idesc(FMT, false, B_MN && !X3, 2 * kBlockM, kPairN);
+    static_assert(!(kTf32 && B_MN && !X3), "packed tf32 operands are K-major");
+    static_assert(!X3 || kTf32, "the in-kernel split is for fp32 operands");
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + Cfg::kStages * Cfg::kStageBytes);
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * Cfg::kStages + 5 + kEpilogueWarps);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + Cfg::kRingBytes);
+    uint32_t *tmem_slot =
+        reinterpret_cast<uint32_t *>(bars + 2 * Cfg::kStages + 5 + kEpilogueWarps + 2 * Cfg::kRawStages);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
@@ -896,11 +942,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * Cfg::kStages + 2 + a); };
     const uint32_t drain_bar = bar0 + 8u * (2 * Cfg::kStages + 4);
     auto fold_bar = [&](int g) { return bar0 + 8u * (2 * Cfg::kStages + 5 + g); };  // stream-K landing, per epilogue warp
+    // X3: the raw ring's barriers (this CTA's own TMA loads / its converters)
+    auto raw_full_bar = [&](int r) { return bar0 + 8u * (2 * Cfg::kStages + 5 + kEpilogueWarps + r); };
+    auto raw_empty_bar = [&](int r) {
+        return bar0 + 8u * (2 * Cfg::kStages + 5 + kEpilogueWarps + Cfg::kRawStages + r);
+    };
+    // X3 stage s of the MMA ring: [A hi | A lo | B hi | B lo]; raw stage r: [A | B]
+    auto raw_of = [&](int r) { return smem + Cfg::kStages * Cfg::kStageBytes + r * Cfg::kRawStageBytes; };
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < Cfg::kStages; ++s) {
-            mbar_init(full_bar(s), 1);
+            // X3: full[s] of the even CTA counts every converter warp of the pair
+            mbar_init(full_bar(s), X3 ? 2 * kX3ConvWarps : 1);
             mbar_init(empty_bar(s), 1);
+        }
+        for (int r = 0; r < Cfg::kRawStages; ++r) {
+            mbar_init(raw_full_bar(r), 1);
+            mbar_init(raw_empty_bar(r), kX3ConvWarps);
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(tfull_bar(a), 1);
@@ -933,7 +991,140 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     sched.init(p, pair, num_pairs, total);
     PairWork w;
 
-    if (warp == 0) {
+    if (X3 && warp == 0) {
+        // ------------------------------------------------ TMA producer, raw fp32 tiles (both CTAs)
+        if (lane == 0) {
+            const uint64_t pol_a = operand_l2_policy_a(), pol_b = operand_l2_policy_b();
+            int r = 0;
+            uint32_t ph = 0;
+            bool ok = true;
+            PairUnits units;
+            units.init(sched, pair);
+            while (ok && units.next(sched, w)) {
+                int64_t tm, tn;
+                tile_raster(num_m_pairs, num_n_pairs, kGroupM, w.tile, tm, tn);
+                const int m0 = static_cast<int>(tm) * 2 * kBlockM + static_cast<int>(rank) * kBlockM;
+                const int n0 = static_cast<int>(tn) * kPairN + static_cast<int>(rank) * kPairHalfN;
+                const bool rev = p.k_snake && w.tile < sched.dp_tiles && ((w.tile - pair) / num_pairs) & 1;
+                for (int kb = w.k0; kb < w.k1; ++kb) {
+                    if (!mbar_wait(raw_empty_bar(r), ph ^ 1u, abort_flag, p.timeout_ns)) {
+                        ok = false;
+                        break;
+                    }
+                    const int kx = (rev ? w.k0 + w.k1 - 1 - kb : kb) * kBK;
+                    const uint32_t sa = smem_addr(raw_of(r)), sb = sa + X3PairCfg::kABytes;
+                    mbar_arrive_expect_tx(raw_full_bar(r), X3PairCfg::kRawStageBytes);
+                    tma_load_2d(sa, &tmap_a, raw_full_bar(r), kx, m0, pol_a);
+                    if constexpr (B_MN) {  // four 32-column x 32-K boxes, N contiguous
+#pragma unroll
+                        for (int j = 0; j < kPairHalfN / 32; ++j)
+                            tma_load_2d(sb + j * (kBK * 128), &tmap_b, raw_full_bar(r), n0 + 32 * j, kx, pol_b);
+                    } else {
+                        tma_load_2d(sb, &tmap_b, raw_full_bar(r), kx, n0, pol_b);
+                    }
+                    if (++r == Cfg::kRawStages) {
+                        r = 0;
+                        ph ^= 1u;
+                    }
+                }
+            }
+            if (!ok) {
+                *abort_flag = 1;
+                atomicExch(p.err, kDevAbortGemmProducer);
+            }
+        }
+    } else if (X3 && warp >= kThreads / 32) {
+        // ------------------------------------------------ converter warps (both CTAs): raw -> tf32 hi / lo
+        const int cw = warp - kThreads / 32;
+        const int tid = cw * 32 + lane;
+        const uint32_t even_full0 = map_to_rank(full_bar(0), 0);
+        int r = 0, s = 0, round = 0;
+        uint32_t rph = 0, sph = 0;
+        bool ok = true;
+        PairUnits units;
+        units.init(sched, pair);
+        while (ok && units.next(sched, w)) {
+            for (int kb = w.k0; kb < w.k1; ++kb) {
+                // MMA stage s free (the pair's MMAs of its last round have read it;
+                // the even CTA's first converter forwards that to the odd CTA)
+                bool ready = mbar_wait(empty_bar(s), sph ^ 1u, abort_flag, p.timeout_ns);
+                if (ready && even && cw == 0 && lane == 0 && round > 0)
+                    mbar_arrive_cluster(map_to_rank(empty_bar(s), 1));
+                ready = ready && mbar_wait(raw_full_bar(r), rph, abort_flag, p.timeout_ns);
+                if (!__all_sync(0xffffffffu, ready)) {
+                    ok = false;
+                    break;
+                }
+                const uint8_t *raw = raw_of(r);
+                uint8_t *st_ = smem + s * Cfg::kStageBytes;
+                // A: the same swizzled layout in and out, 16-byte chunk by chunk
+#pragma unroll
+                for (int q = 0; q < X3PairCfg::kABytes / 16 / (32 * kX3ConvWarps); ++q) {
+                    const int c = tid + q * 32 * kX3ConvWarps;
+                    const float4 x = reinterpret_cast<const float4 *>(raw)[c];
+                    float4 hi, lo;
+                    split4(x, hi, lo);
+                    reinterpret_cast<float4 *>(st_)[c] = hi;
+                    reinterpret_cast<float4 *>(st_ + X3PairCfg::kABytes)[c] = lo;
+                }
+                const uint8_t *rawb = raw + X3PairCfg::kABytes;
+                uint8_t *bhi = st_ + 2 * X3PairCfg::kABytes, *blo = bhi + X3PairCfg::kBBytes;
+                if constexpr (B_MN) {
+                    // raw box j holds columns [32 j, 32 j + 32) x 32 K rows, N contiguous:
+                    // element (n = 32 j + t, k) at k * 128 + ((t / 4) ^ (k % 8)) * 16 + (t % 4) * 4,
+                    // so lane t reading column t of one K row hits bank 4 ((t / 4) ^ (k % 8)) + t % 4,
+                    // 32 distinct banks.  Lane t takes K rows 4 kq .. 4 kq + 3 of column t and
+                    // writes them as one 16-byte chunk of row n of the K-major tile, at
+                    // n * 128 + (kq ^ (n % 8)) * 16: 8 distinct chunks per quarter warp.
+#pragma unroll
+                    for (int t = 0; t < 32 / kX3ConvWarps; ++t) {
+                        const int combo = cw * (32 / kX3ConvWarps) + t;
+                        const int j = combo >> 3, kq = combo & 7;
+                        const uint8_t *box = rawb + j * (kBK * 128) + ((lane & 3) << 2);
+                        float v[4];
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            const int k = 4 * kq + i;
+                            v[i] = *reinterpret_cast<const float *>(box + k * 128 + (((lane >> 2) ^ (k & 7)) << 4));
+                        }
+                        const int n = 32 * j + lane;
+                        float4 hi, lo;
+                        split4(make_float4(v[0], v[1], v[2], v[3]), hi, lo);
+                        const int off = n * 128 + ((kq ^ (n & 7)) << 4);
+                        *reinterpret_cast<float4 *>(bhi + off) = hi;
+                        *reinterpret_cast<float4 *>(blo + off) = lo;
+                    }
+                } else {
+#pragma unroll
+                    for (int q = 0; q < X3PairCfg::kBBytes / 16 / (32 * kX3ConvWarps); ++q) {
+                        const int c = tid + q * 32 * kX3ConvWarps;
+                        const float4 x = reinterpret_cast<const float4 *>(rawb)[c];
+                        float4 hi, lo;
+                        split4(x, hi, lo);
+                        reinterpret_cast<float4 *>(bhi)[c] = hi;
+                        reinterpret_cast<float4 *>(blo)[c] = lo;
+                    }
+                }
+                fence_proxy_async_smem();  // these generic writes -> the tensor core's reads
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(raw_empty_bar(r));
+                    if (even) mbar_arrive_release_cluster(full_bar(s));
+                    else mbar_arrive_cluster_release(even_full0 + 8u * s);
+                }
+                if (++r == Cfg::kRawStages) {
+                    r = 0;
+                    rph ^= 1u;
+                }
+                if (++s == Cfg::kStages) {
+                    s = 0;
+                    sph ^= 1u;
+                    ++round;
+                }
+            }
+        }
+        if (!ok) *abort_flag = 1;
+    } else if (warp == 0) {
         // ------------------------------------------------ TMA producer (both CTAs)
         if (lane == 0) {
             const uint64_t pol_a = operand_l2_policy_a(), pol_b = operand_l2_policy_b();
@@ -1003,23 +1194,42 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 tc_fence_after_sync();
                 const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kPairN);
                 for (int kb = w.k0; kb < w.k1; ++kb) {
-                    if (!mbar_wait(full_bar(s), ph, abort_flag, p.timeout_ns)) {
+                    // X3: the converter warps of both CTAs release their writes at cluster scope
+                    const bool landed = X3 ? mbar_wait_cluster(full_bar(s), ph, abort_flag, p.timeout_ns)
+                                           : mbar_wait(full_bar(s), ph, abort_flag, p.timeout_ns);
+                    if (!landed) {
                         ok = false;
                         break;
                     }
                     tc_fence_after_sync();
                     const uint32_t sa = smem_addr(smem + s * Cfg::kStageBytes);
-                    const uint32_t sb = sa + Cfg::kABytes;
+                    if constexpr (X3) {
+                        const uint32_t salo = sa + X3PairCfg::kABytes, sbhi = sa + 2 * X3PairCfg::kABytes;
+                        const uint32_t sblo = sbhi + X3PairCfg::kBBytes;
 #pragma unroll
-                    for (int ks = 0; ks < kKSteps; ++ks) {
-                        const uint64_t adesc = smem_desc_sw128(sa + ks * 32, 16, 1024);
-                        uint64_t bdesc;
-                        if constexpr (B_MN) {
-                            bdesc = smem_desc_sw128(sb + ks * (kMmaK * 128), kBK * 128, 1024);
-                        } else {
-                            bdesc = smem_desc_sw128(sb + ks * 32, 16, 1024);
+                        for (int ks = 0; ks < kKSteps; ++ks) {
+                            const uint64_t ahi = smem_desc_sw128(sa + ks * 32, 16, 1024);
+                            const uint64_t alo = smem_desc_sw128(salo + ks * 32, 16, 1024);
+                            const uint64_t bh = smem_desc_sw128(sbhi + ks * 32, 16, 1024);
+                            const uint64_t bl = smem_desc_sw128(sblo + ks * 32, 16, 1024);
+                            // the small terms first, then the leading product
+                            tc_mma_pair<true>(d_tmem, alo, bh, kIdesc, (kb != w.k0 || ks != 0) ? 1u : 0u);
+                            tc_mma_pair<true>(d_tmem, ahi, bl, kIdesc, 1u);
+                            tc_mma_pair<true>(d_tmem, ahi, bh, kIdesc, 1u);
                         }
-                        tc_mma_pair<kTf32>(d_tmem, adesc, bdesc, kIdesc, (kb != w.k0 || ks != 0) ? 1u : 0u);
+                    } else {
+                        const uint32_t sb = sa + Cfg::kABytes;
+#pragma unroll
+                        for (int ks = 0; ks < kKSteps; ++ks) {
+                            const uint64_t adesc = smem_desc_sw128(sa + ks * 32, 16, 1024);
+                            uint64_t bdesc;
+                            if constexpr (B_MN) {
+                                bdesc = smem_desc_sw128(sb + ks * (kMmaK * 128), kBK * 128, 1024);
+                            } else {
+                                bdesc = smem_desc_sw128(sb + ks * 32, 16, 1024);
+                            }
+                            tc_mma_pair<kTf32>(d_tmem, adesc, bdesc, kIdesc, (kb != w.k0 || ks != 0) ? 1u : 0u);
+                        }
                     }
                     tc_commit_pair(empty_bar(s));
                     if (++s == Cfg::kStages) {
@@ -1040,7 +1250,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     } else {
         // ------------------------------------------------ epilogue (warps 2..5, both CTAs)
         const int g = warp & 3;
-        const uint32_t staging = smem_addr(smem + Cfg::kStages * Cfg::kStageBytes + kBarRegion) +
+        const uint32_t staging = smem_addr(smem + Cfg::kRingBytes + kBarRegion) +
                                  static_cast<uint32_t>(g * 2 * kStageBoxBytes);
         int sbuf = 0;
         const uint32_t even_tempty0 = map_to_rank(tempty_bar(0), 0);
@@ -1649,10 +1859,11 @@ int launch_c_preset_f32(const GemmArgs &g, const KParams &kp, int pairs, int sm_
 
 // preset: for an L2-add launch whose C is not preset yet, the call whose
 // split tiles get C = 0 + bias first (on the pair count actually launched)
-template <int FMT, bool B_MN>
+template <int FMT, bool B_MN, bool X3 = false>
 int launch_pair(const CUtensorMap &ma, const CUtensorMap &mb, const KParams &kp, const CStoreMaps &cm,
                 int pairs_wanted, const GemmArgs *preset, int sm_count, cudaStream_t stream) {
-    auto kern = gemm_tc_pair_kernel<FMT, B_MN>;
+    using Cfg = std::conditional_t<X3, X3PairCfg, PairCfg>;
+    auto kern = gemm_tc_pair_kernel<FMT, B_MN, X3>;
     static uint64_t attr_set = 0;
     static int max_clusters[64] = {0};
     int dev = 0;
@@ -1660,11 +1871,11 @@ int launch_pair(const CUtensorMap &ma, const CUtensorMap &mb, const KParams &kp,
     const bool cached = dev >= 0 && dev < 64 && (attr_set & (1ull << dev));
     int clusters = cached ? max_clusters[dev] : 0;
     if (!cached) {
-        ST_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, PairCfg::kSmemBytes));
+        ST_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(2 * pairs_wanted, 1, 1);
-        cfg.blockDim = dim3(kThreads, 1, 1);
-        cfg.dynamicSmemBytes = PairCfg::kSmemBytes;
+        cfg.blockDim = dim3(Cfg::kThreadCount, 1, 1);
+        cfg.dynamicSmemBytes = Cfg::kSmemBytes;
         cudaLaunchAttribute attr;
         attr.id = cudaLaunchAttributeClusterDimension;
         attr.val.clusterDim.x = 2;
@@ -1685,8 +1896,8 @@ int launch_pair(const CUtensorMap &ma, const CUtensorMap &mb, const KParams &kp,
     if (preset != nullptr) ST_TRY(launch_c_preset_f32(*preset, kp, pairs, sm_count, stream));
     if (std::getenv("SPTILES_B200_DEBUG"))
         std::fprintf(stderr, "[sptiles_b200] pair gemm: %d pairs (wanted %d, co-resident clusters %d), smem %d\n",
-                     pairs, pairs_wanted, clusters, PairCfg::kSmemBytes);
-    ST_CUDA_TRY(launch_kernel(kern, 2 * pairs, kThreads, PairCfg::kSmemBytes, stream, ma, mb, kp, cm));
+                     pairs, pairs_wanted, clusters, Cfg::kSmemBytes);
+    ST_CUDA_TRY(launch_kernel(kern, 2 * pairs, Cfg::kThreadCount, Cfg::kSmemBytes, stream, ma, mb, kp, cm));
     note_launch();
     const cudaError_t e = cudaPeekAtLastError();
     return e == cudaSuccess ? ST_OK : cuda_fail(cudaGetLastError(), "gemm_tc_pair_kernel launch");
@@ -1818,15 +2029,16 @@ size_t stream_k_workspace_bytes(int sm_count) {
     return stream_k_flag_offset(sm_count) + static_cast<size_t>(pairs) * 2 * 2 * kEpilogueWarps * sizeof(int);
 }
 
-int plan_gemm(int in_dtype, int64_t m, int64_t n, int64_t k, int sm_count, GemmPlan *plan, int sk_mode) {
+int plan_gemm(int in_dtype, int64_t m, int64_t n, int64_t k, int sm_count, GemmPlan *plan, int sk_mode,
+              bool force_pair) {
     if (sk_mode < 0) sk_mode = stream_k_mode();
     if (m <= 0 || n <= 0 || k <= 0) return fail(ST_ERR_INVALID_ARGUMENT, "matmul extents must be positive");
     if (sm_count <= 0) sm_count = 148;
     // SPTILES_B200_GEMM_KERNEL=pair|single pins the kernel family (tests use it
     // to cover both on every shape); unset, the scores below decide
     const char *force = std::getenv("SPTILES_B200_GEMM_KERNEL");
-    const bool only_pair = force && std::strcmp(force, "pair") == 0;
-    const bool only_single = force && std::strcmp(force, "single") == 0;
+    const bool only_pair = force_pair || (force && std::strcmp(force, "pair") == 0);
+    const bool only_single = !force_pair && force && std::strcmp(force, "single") == 0;
     GemmPlan best;
     double best_score = -1.0;
     // one CTA per SM: block 128 x {256, 128, 64}; relative tensor-pipe
@@ -1949,7 +2161,8 @@ int stream_k_fold(const GemmArgs &g, int sm_count) {
     const int mode = stream_k_mode_for(g);
     if (mode <= 0) return kFoldNone;
     GemmPlan plan;
-    if (plan_gemm(g.ab_dtype, g.m, g.n, g.k, sm_count, &plan, mode) != ST_OK || !plan.pair) return kFoldNone;
+    if (plan_gemm(g.ab_dtype, g.m, g.n, g.k, sm_count, &plan, mode, g.split_fp32) != ST_OK || !plan.pair)
+        return kFoldNone;
     if (sm_count <= 0) sm_count = 148;
     int dp = 0, skp = 0;
     long long ski = 0;
@@ -1958,11 +2171,40 @@ int stream_k_fold(const GemmArgs &g, int sm_count) {
     return stream_k_l2add_ok(g) ? kFoldL2Add : kFoldExchange;
 }
 
+// SPTILES_B200_SK_FOLD=preset: the L2 fold presets C even where it would be ordered.
+bool sk_ordered_enabled() {
+    const char *v = std::getenv("SPTILES_B200_SK_FOLD");
+    return !(v != nullptr && std::strcmp(v, "preset") == 0);
+}
+
+// The L2 fold of a launch whose split tiles fold by L2 reduce-add (0 when
+// they do not): 2, ordered -- a tile's first unit stores, the others add
+// after its flags -- when whole-tile waves come before the split tiles, so
+// the first units finish long before the last ones and nothing waits; 1,
+// every unit adds onto C preset to the bias, when every tile is split: the
+// units then finish together, and an ordered fold would put a store, a flag
+// and the adds in a row (fp32 1024^3: 27 vs 22 us per call).
+int stream_k_l2add_mode(const GemmArgs &g, int sm_count) {
+    if (stream_k_fold(g, sm_count) != kFoldL2Add) return 0;
+    if (!sk_ordered_enabled()) return 1;
+    GemmPlan plan;
+    const int mode = stream_k_mode_for(g);
+    if (plan_gemm(g.ab_dtype, g.m, g.n, g.k, sm_count, &plan, mode, g.split_fp32) != ST_OK) return 1;
+    if (sm_count <= 0) sm_count = 148;
+    int dp = 0, skp = 0;
+    long long ski = 0;
+    stream_k_split(plan.tiles, sm_count / 2, static_cast<int>(cdiv(g.k, plan.block_k)), mode, dp, skp, ski);
+    return dp > 0 ? 2 : 1;
+}
+
 // Whether launch_gemm uses the stream-K workspace: the exchange folds
 // through its partials and flags, the ordered L2 fold through its flags (the
 // workspace is only acquired then, so other calls put no event between
 // their launches).
-bool gemm_uses_stream_k(const GemmArgs &g, int sm_count) { return stream_k_fold(g, sm_count) != kFoldNone; }
+bool gemm_uses_stream_k(const GemmArgs &g, int sm_count) {
+    const int fold = stream_k_fold(g, sm_count);
+    return fold == kFoldExchange || (fold == kFoldL2Add && stream_k_l2add_mode(g, sm_count) == 2);
+}
 
 // C[r, q] = 0 + bias[q] (0 without a bias) for r < m, q < n: the value the
 // split units of an L2-add stream-K launch add their partial tiles onto.
@@ -2011,10 +2253,16 @@ int preload_gemm_tf32_kernels() {
     return ST_OK;
 }
 
-// SPTILES_B200_SK_FOLD=preset: the L2 fold presets C even when flags exist.
-bool sk_ordered_enabled() {
-    const char *v = std::getenv("SPTILES_B200_SK_FOLD");
-    return !(v != nullptr && std::strcmp(v, "preset") == 0);
+bool gemm_split_fp32_fits(const GemmArgs &g, int sm_count) {
+    // where the packed route (K' = 3 roundup(K, 32)) would run CTA pairs, the
+    // same kernel splitting in shared memory does the same MMAs without the pack
+    GemmPlan plan;
+    if (plan_gemm(ST_F32, g.m, g.n, 3 * tf32_packed_k(g.k), sm_count, &plan, stream_k_mode_for(g)) != ST_OK ||
+        !plan.pair)
+        return false;
+    for (const void *ptr : {g.a, g.b})
+        if (reinterpret_cast<uintptr_t>(ptr) % 16 != 0) return false;
+    return (g.lda * 4) % 16 == 0 && (g.ldb * 4) % 16 == 0;
 }
 
 // SPTILES_B200_K_SNAKE=0 keeps every tile's K order ascending.
@@ -2027,11 +2275,14 @@ int launch_gemm(const GemmArgs &g, int sm_count, int *dev_err, uint64_t timeout_
     GemmPlan plan;
     // the packed tf32 K already includes the 3x expansion; plan on the product extents
     const int sk_mode = stream_k_mode_for(g);
-    ST_TRY(plan_gemm(g.ab_dtype, g.m, g.n, g.k, sm_count, &plan, sk_mode));
+    ST_TRY(plan_gemm(g.ab_dtype, g.m, g.n, g.k, sm_count, &plan, sk_mode, g.split_fp32));
     const bool tf32 = g.ab_dtype == ST_F32;
     const int elem = tf32 ? 4 : 2;
     const int bk = kRowBytes / elem;
-    if (g.b_k_major == false && tf32) return fail(ST_ERR_UNSUPPORTED, "tf32 B operand must be K-major");
+    if (g.split_fp32 && (!tf32 || !plan.pair))
+        return fail(ST_ERR_UNSUPPORTED, "the in-kernel 3xTF32 split runs on the CTA-pair kernel only");
+    if (g.b_k_major == false && tf32 && !g.split_fp32)
+        return fail(ST_ERR_UNSUPPORTED, "tf32 B operand must be K-major");
     for (const void *p : {g.a, g.b})
         if (reinterpret_cast<uintptr_t>(p) % 16 != 0)
             return fail(ST_ERR_INVALID_ARGUMENT, "tensor-core operands must be 16-byte aligned");
@@ -2047,8 +2298,10 @@ int launch_gemm(const GemmArgs &g, int sm_count, int *dev_err, uint64_t timeout_
         ST_TRY(make_map(&mb, dt, g.b, static_cast<uint64_t>(g.k), static_cast<uint64_t>(g.n),
                         static_cast<uint64_t>(g.ldb) * elem, bk, plan.pair ? kPairHalfN : plan.block_n));
     } else {
+        // N-contiguous B: boxes of 64 16-bit columns, or (raw fp32 for the
+        // in-kernel split) 32 columns of 128 bytes x 32 K rows
         ST_TRY(make_map(&mb, dt, g.b, static_cast<uint64_t>(g.n), static_cast<uint64_t>(g.k),
-                        static_cast<uint64_t>(g.ldb) * elem, 64, bk));
+                        static_cast<uint64_t>(g.ldb) * elem, g.split_fp32 ? 32 : 64, bk));
     }
     KParams kp;
     kp.m = static_cast<int>(g.m);
@@ -2069,8 +2322,11 @@ int launch_gemm(const GemmArgs &g, int sm_count, int *dev_err, uint64_t timeout_
     kp.timeout_ns = timeout_ns;
     const int fold = plan.pair ? stream_k_fold(g, sm_count) : kFoldNone;
     kp.sk_mode = sk_mode;
-    // the ordered L2 fold needs the stream-K flags; without them C is preset
-    kp.sk_l2add = fold == kFoldL2Add ? (g.sk_flags != nullptr && sk_ordered_enabled() ? 2 : 1) : 0;
+    // the ordered L2 fold needs the stream-K flags; without them (or with C
+    // already preset by the caller) every unit adds onto a preset C
+    kp.sk_l2add = 0;
+    if (fold == kFoldL2Add)
+        kp.sk_l2add = stream_k_l2add_mode(g, sm_count) == 2 && g.sk_flags != nullptr && !g.c_preset ? 2 : 1;
     kp.k_snake = k_snake_enabled() ? 1 : 0;
     kp.sk_ws = fold == kFoldExchange ? g.sk_ws : nullptr;
     kp.sk_flags = fold != kFoldNone ? g.sk_flags : nullptr;
@@ -2097,6 +2353,9 @@ int launch_gemm(const GemmArgs &g, int sm_count, int *dev_err, uint64_t timeout_
         if (g.ab_dtype == ST_BF16)
             return g.b_k_major ? launch_pair<1, false>(ma, mb, kp, cm, pairs, preset, sms, stream)
                                : launch_pair<1, true>(ma, mb, kp, cm, pairs, preset, sms, stream);
+        if (g.split_fp32)
+            return g.b_k_major ? launch_pair<2, false, true>(ma, mb, kp, cm, pairs, preset, sms, stream)
+                               : launch_pair<2, true, true>(ma, mb, kp, cm, pairs, preset, sms, stream);
         return launch_pair<2, false>(ma, mb, kp, cm, pairs, preset, sms, stream);
     }
     if (g.ab_dtype == ST_F16) {

@@ -397,6 +397,29 @@ int matmul_device(const ExecCtx &x, const st_tensor &a, const st_tensor &b, cons
             g.k = K;
             return launch_gemm_3xtf32(g, x.dev->sm_count, x.dev->dev_err, kDeviceWaitLimitNs, x.stream);
         }
+        // Opt-in (SPTILES_B200_FP32=split): operands TMA can address in place, on
+        // a CTA-pair plan, are split into tf32 hi / lo by the pair kernel itself,
+        // with no packing pass.  Its converter traffic makes it shared-memory
+        // bound (~70 % of the MMA rate): it ties with packing at 1024^3 and
+        // loses from 2048^3 up (750 vs 578 us at 4096^3), so packing is the default.
+        const char *route = std::getenv("SPTILES_B200_FP32");
+        if (route && std::strcmp(route, "split") == 0 && a_ok && (b_rows_ok || b_cols_ok)) {
+            GemmArgs gs = g;
+            gs.ab_dtype = ST_F32;
+            gs.a = a.data;
+            gs.lda = a.strides[0];
+            gs.b = b.data;
+            gs.b_k_major = !b_rows_ok;
+            gs.ldb = b_rows_ok ? b.strides[0] : b.strides[1];
+            gs.k = K;
+            gs.split_fp32 = true;
+            if (gemm_split_fp32_fits(gs, x.dev->sm_count)) {
+                if (gemm_uses_stream_k(gs, x.dev->sm_count)) ST_TRY(sk_acquire(x.dev, x.stream, gs));
+                ST_TRY(launch_gemm(gs, x.dev->sm_count, x.dev->dev_err, kDeviceWaitLimitNs, x.stream));
+                if (gs.sk_ws) ST_TRY(ws_release(x.dev->sk, x.stream));
+                return ST_OK;
+            }
+        }
         // otherwise pack [hi|hi|lo] x [hi;lo;hi] into scratch and run one tf32 GEMM
         const int64_t kp = tf32_packed_k(K);
         const size_t need = static_cast<size_t>(M + N) * 3 * kp * sizeof(float);
@@ -411,13 +434,13 @@ int matmul_device(const ExecCtx &x, const st_tensor &a, const st_tensor &b, cons
         g.ldb = 3 * kp;
         g.b_k_major = true;
         g.k = 3 * kp;
-        // split tiles fold through the stream-K workspace's flags; an L2-add
-        // launch without them (a capture before the workspace exists) starts
-        // from C = bias, which the pack writes
-        const int fold = stream_k_fold(g, x.dev->sm_count);
-        if (fold != kFoldNone) ST_TRY(sk_acquire(x.dev, x.stream, g));
+        // split tiles that fold in L2 onto a preset C start from C = bias,
+        // which the pack writes; the ordered fold and the exchange use the
+        // stream-K workspace (an ordered launch captured before the workspace
+        // exists presets C by its own kernel instead)
+        if (gemm_uses_stream_k(g, x.dev->sm_count)) ST_TRY(sk_acquire(x.dev, x.stream, g));
         CPreset preset;
-        if (fold == kFoldL2Add && g.sk_flags == nullptr) {
+        if (stream_k_l2add_mode(g, x.dev->sm_count) == 1) {
             preset.c = static_cast<float *>(c.data);
             preset.ldc = c.strides[0];
             preset.bias = bias_ptr;

@@ -282,6 +282,44 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
     asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 
+// Arrive on an mbarrier in another CTA of the cluster, releasing this
+// thread's earlier writes at cluster scope: for arrivals that announce data
+// the arriving threads wrote into their own shared memory for the partner.
+__device__ __forceinline__ void mbar_arrive_cluster_release(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+// A local arrive with the same cluster-scope release.
+__device__ __forceinline__ void mbar_arrive_release_cluster(uint32_t bar) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+// mbar_wait with cluster-scope acquire: pairs with the arrivals above.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+__device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity, const volatile int *abort_flag,
+                                                  uint64_t limit_ns) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    const uint64_t t0 = global_timer_ns();
+    for (uint32_t i = 1;; ++i) {
+        if (mbar_try_wait_cluster(bar, parity)) return true;
+        if ((i & 31u) == 0u) {
+            if (*abort_flag) return false;
+            if (global_timer_ns() - t0 > limit_ns) return false;
+        }
+    }
+}
+
 // 2D tiled load into this CTA's shared memory whose completion is counted on
 // `bar_cluster`, an mbarrier in either CTA of the pair (shared::cluster address).
 __device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap *map, uint32_t bar_cluster, int32_t c0,

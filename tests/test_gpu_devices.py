@@ -85,7 +85,7 @@ def test_all_devices_runs_on_the_contexts_streams():
 
 @needs_two
 def test_fused_allgather_between_devices_of_one_process():
-    devs = ALL[:2]
+    devs = ALL[:8]
     ctx = st.context_group(devs)
     m, n, k = 3000, 1024, 512
     a, b = kat(m, n, k)

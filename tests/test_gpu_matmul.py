@@ -410,16 +410,28 @@ def test_calls_replay_from_a_cuda_graph(dtype):
 
 
 # ------------------------------------------------------------ fp32: split in the kernel vs packed operands
-@pytest.mark.parametrize("path", ["fused", "prepack"])
-@pytest.mark.parametrize("mnk", [(64, 64, 64), (100, 72, 36), (300, 520, 200), (1000, 24, 520), (516, 780, 132),
-                                 (1024, 1024, 1024), (100, 70, 33)])
-def test_fp32_paths_known_answers(monkeypatch, path, mnk):
-    """The default route packs [hi|hi|lo] x [hi;lo;hi] and runs one tf32 GEMM;
-    the opt-in fused kernel splits TMA-staged fp32 tiles in shared memory."""
+FP32_PATHS = ["split", "pack", "fused"]
+
+
+def fp32_path(monkeypatch, path):
+    """pack: [hi|hi|lo] x [hi;lo;hi] packed in global memory, then one tf32
+    GEMM (the default); split: the CTA-pair kernel splits raw fp32 tiles into
+    tf32 hi / lo itself (opt-in; shapes whose plan is not CTA pairs still
+    pack); fused: the opt-in one-CTA kernel that splits in shared memory."""
+    monkeypatch.delenv("SPTILES_B200_FP32_FUSED", raising=False)
+    monkeypatch.delenv("SPTILES_B200_FP32", raising=False)
     if path == "fused":
         monkeypatch.setenv("SPTILES_B200_FP32_FUSED", "1")
-    else:
-        monkeypatch.delenv("SPTILES_B200_FP32_FUSED", raising=False)
+    elif path == "split":
+        monkeypatch.setenv("SPTILES_B200_FP32", "split")
+
+
+@pytest.mark.parametrize("path", FP32_PATHS)
+@pytest.mark.parametrize("mnk", [(64, 64, 64), (100, 72, 36), (300, 520, 200), (1000, 24, 520), (516, 780, 132),
+                                 (1024, 1024, 1024), (100, 70, 33), (2048, 2048, 512), (1536, 1000, 700),
+                                 (4096, 2048, 96)])
+def test_fp32_paths_known_answers(monkeypatch, path, mnk):
+    fp32_path(monkeypatch, path)
     m, n, k = mnk
     A, B = kat(m, n, k, torch.float32)
     want = oracle.matmul_kat_expected(m, n, k).tobytes()
@@ -427,12 +439,9 @@ def test_fp32_paths_known_answers(monkeypatch, path, mnk):
     assert st.matmul(A, B.t().contiguous().t()).cpu().numpy().tobytes() == want  # column-major B
 
 
-@pytest.mark.parametrize("path", ["fused", "prepack"])
+@pytest.mark.parametrize("path", FP32_PATHS)
 def test_fp32_paths_random_accuracy(monkeypatch, path):
-    if path == "fused":
-        monkeypatch.setenv("SPTILES_B200_FP32_FUSED", "1")
-    else:
-        monkeypatch.delenv("SPTILES_B200_FP32_FUSED", raising=False)
+    fp32_path(monkeypatch, path)
     m, n, k = 768, 640, 1000
     A, B = normal((m, k), 1.0, 80, torch.float32), normal((k, n), 1.0, 81, torch.float32)
     bias = normal((n,), 1.0, 82, torch.float32)
@@ -441,6 +450,79 @@ def test_fp32_paths_random_accuracy(monkeypatch, path):
         C = st.matmul(A, Bv, bias)
         err = rel_err(C.cpu().numpy(), want)
         assert err <= 5e-5, f"{path}: 3xTF32 error {err}"
+
+
+@pytest.mark.parametrize("fold", ["ordered", "preset", "exchange", "whole"])
+@pytest.mark.parametrize("mnk", [(1024, 1024, 1024), (2048, 3000, 700), (3000, 5000, 520)],
+                         ids=lambda s: "x".join(map(str, s)))
+def test_fp32_split_stream_k_folds(monkeypatch, fold, mnk):
+    """The in-kernel split on every fold of split tiles (1024^3: every tile
+    split; the others: whole-tile waves and a split last wave), against the
+    packed route and the oracle, with a bias; N-contiguous and K-major B."""
+    monkeypatch.setenv("SPTILES_B200_GEMM_KERNEL", "pair")
+    fp32_path(monkeypatch, "split")
+    if fold == "preset":
+        monkeypatch.setenv("SPTILES_B200_SK_FOLD", "preset")
+    elif fold == "exchange":
+        monkeypatch.setenv("SPTILES_B200_SK_FOLD", "exchange")
+        monkeypatch.setenv("SPTILES_B200_STREAM_K", "2")
+    elif fold == "whole":
+        monkeypatch.setenv("SPTILES_B200_STREAM_K", "0")
+    m, n, k = mnk
+    Ak, Bk = kat(m, n, k, torch.float32)
+    want = oracle.matmul_kat_expected(m, n, k).tobytes()
+    assert st.matmul(Ak, Bk).cpu().numpy().tobytes() == want
+    assert st.matmul(Ak, Bk.t().contiguous().t()).cpu().numpy().tobytes() == want
+    A, B = normal((m, k), 1.0, 83, torch.float32), normal((k, n), 1.0, 84, torch.float32)
+    bias = normal((n,), 1.0, 85, torch.float32)
+    C = st.matmul(A, B, bias)
+    rows = (m - 64, m)
+    assert rel_err(C[rows[0]:rows[1]].cpu().numpy(), oracle_mm(A, B, bias, rows=rows)) <= 5e-5
+    assert full_rel_err(C, fp64_product(A, B, bias)) <= 5e-5
+    fp32_path(monkeypatch, "pack")
+    Cp = st.matmul(A, B, bias)
+    assert rel_err(C.cpu().numpy(), Cp.cpu().numpy()) <= 5e-5
+
+
+@pytest.mark.parametrize("out_dtype", [torch.float16, torch.bfloat16], ids=["f16", "bf16"])
+def test_fp32_split_16bit_out(monkeypatch, out_dtype):
+    fp32_path(monkeypatch, "split")
+    m, n, k = 1024, 1536, 800
+    A, B = normal((m, k), 1.0, 86, torch.float32), normal((k, n), 1.0, 87, torch.float32)
+    bias = normal((n,), 1.0, 88, torch.float32)
+    C = st.matmul(A, B, bias, out_dtype=out_dtype)
+    ref = fp64_product(A, B, bias)
+    assert full_rel_err(C, ref) <= 1e-2
+    d = (C.double() - ref).abs()
+    step = 2.0 ** -10 if out_dtype == torch.float16 else 2.0 ** -7  # one rounding step, relative
+    assert bool((d <= ref.abs() * step + 1e-4 * ref.abs().max()).all())
+
+
+def test_fp32_split_config_every_row_and_graph_replay(monkeypatch):
+    """The fp32 configuration (1024^3, N(0, 1)): every element against fp64,
+    the oracle on row samples, deterministic mode bit for bit, and a CUDA
+    graph replay of the call."""
+    fp32_path(monkeypatch, "split")
+    A, B = normal((1024, 1024), 1.0, 2, torch.float32), normal((1024, 1024), 1.0, 20, torch.float32)
+    C = st.matmul(A, B)
+    assert full_rel_err(C, fp64_product(A, B)) <= 5e-5
+    for r0, r1 in _sample_rows(1024):
+        assert rel_err(C[r0:r1].cpu().numpy(), oracle_mm(A, B, rows=(r0, r1))) <= 5e-5
+    with deterministic():
+        d0, d1 = st.matmul(A, B), st.matmul(A, B)
+    assert torch.equal(d0, d1)
+    assert rel_err(d0.cpu().numpy(), C.cpu().numpy()) <= 5e-5
+    out = torch.empty_like(C)
+    st.matmul(A, B, out=out)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        st.matmul(A, B, out=out)
+    for _ in range(3):
+        out.fill_(float("nan"))
+        g.replay()
+        torch.cuda.synchronize()
+        assert rel_err(out.cpu().numpy(), C.cpu().numpy()) <= 5e-5
 
 
 # ------------------------------------------------------------ stream-K tail of the CTA-pair kernel
@@ -498,17 +580,14 @@ def test_stream_k_exchange_fold_known_answers(monkeypatch, dtype, mnk):
     assert C.cpu().numpy().tobytes() == oracle.matmul_kat_expected(m, n, k).tobytes()
 
 
-@pytest.mark.parametrize("fold", ["ordered", "preset"])
 @pytest.mark.parametrize("dtype", [torch.float32, torch.float16], ids=["f32", "f16"])
 @pytest.mark.parametrize("mnk", [(1024, 1024, 1024), (300, 520, 2000), (1000, 3000, 2000)],
                          ids=lambda s: "x".join(map(str, s)))
-def test_stream_k_l2add_fold_random_bias(monkeypatch, fold, dtype, mnk):
-    """Split tiles added in L2 (onto a first unit's store, or onto C preset to
-    the bias) agree with whole tiles and with the exchange up to summation
-    order, and with the oracle."""
+def test_stream_k_l2add_fold_random_bias(monkeypatch, dtype, mnk):
+    """Every tile split: the units add onto C preset to the bias (by the fp32
+    pack, or a preset kernel); agrees with whole tiles and with the exchange
+    up to summation order, and with the oracle."""
     monkeypatch.setenv("SPTILES_B200_GEMM_KERNEL", "pair")
-    if fold == "preset":
-        monkeypatch.setenv("SPTILES_B200_SK_FOLD", "preset")
     m, n, k = mnk
     A, B = normal((m, k), 0.5, 90, dtype), normal((k, n), 0.5, 91, dtype)
     bias = normal((n,), 1.0, 92, torch.float32)

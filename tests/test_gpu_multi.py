@@ -2,7 +2,8 @@
 
 Each rank computes its M-row block of C with the tensor-core kernels and the
 row blocks are all-gathered into a replicated C; vector_add shards by element
-range.  Needs two visible GPUs (skipped otherwise)."""
+range.  Runs one rank per visible GPU (up to 8); needs two (skipped
+otherwise)."""
 import datetime
 import os
 import socket
@@ -95,26 +96,36 @@ def _worker(rank, world, port, q):
         hB = torch.from_numpy(b).to(torch.bfloat16).pin_memory()
         Ch = sharded_matmul_host(hA, hB, m_total=m, out_dtype=torch.float32)
         out["host_kat"] = Ch.numpy().tobytes() == oracle.matmul_kat_expected(m, n, k)[r0:r1].tobytes()
-        m3, n3, k3 = 300, 200, 1001  # B rows split 501 + 500 (the last slice short and zero padded)
+        m3, n3, k3 = 1100, 200, 1001  # B's rows split unevenly (the last slice short and zero padded)
         a3 = oracle.kat_values(m3 * k3, 17, 8, 0.25).reshape(m3, k3)
         b3 = oracle.kat_values(k3 * n3, 13, 6, 0.5).reshape(k3, n3)
         t0, t1 = matmul_row_shard(m3, world, rank)
         C3 = sharded_matmul_host(torch.from_numpy(a3[t0:t1]).half().pin_memory(), torch.from_numpy(b3).half(),
                                  m_total=m3, out_dtype=torch.float32)
         out["host_kat_odd_k"] = C3.numpy().tobytes() == oracle.matmul_kat_expected(m3, n3, k3)[t0:t1].tobytes()
+        # fewer 128-row blocks than some ranks' share: empty shards (300 rows
+        # over 4 or 8 ranks leave ranks without rows)
+        m6, n6, k6 = 300, 256, 256
+        a6 = oracle.kat_values(m6 * k6, 17, 8, 0.25).reshape(m6, k6)
+        b6 = oracle.kat_values(k6 * n6, 13, 6, 0.5).reshape(k6, n6)
+        v0, v1 = matmul_row_shard(m6, world, rank)
+        C6 = sharded_matmul(torch.from_numpy(a6[v0:v1]).to(dev, torch.float16), torch.from_numpy(b6).to(dev,
+                            torch.float16), m_total=m6, out_dtype=torch.float32, replicate_output=True)
+        out["empty_shards_kat"] = C6.cpu().numpy().tobytes() == oracle.matmul_kat_expected(m6, n6, k6).tobytes()
         q.put((rank, out))
     finally:
         dist.destroy_process_group()
 
 
 @needs_two
-def test_row_sharded_matmul_and_allgather_on_two_gpus():
+def test_row_sharded_matmul_and_allgather_on_every_gpu():
     import torch.multiprocessing as mp
 
+    world = min(torch.cuda.device_count(), 8)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
     results = dict(q.get(timeout=300) for _ in procs)
