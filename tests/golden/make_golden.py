@@ -3,7 +3,7 @@
 Run in a container where the reference tree is mounted (it is read, never
 written):
 
-    python tests/golden/make_golden.py /root/reference
+    python tests/golden/make_golden.py <path of the reference tree>
 
 What is taken from the reference, unmodified, by import:
   * shaders/spirv_runtime.py: LOCAL_SIZE_X, ceil_div, tensor_1d_descriptor,
@@ -115,4 +115,6 @@ def main(ref_root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_golden.py <path of the reference tree>")
+    main(sys.argv[1])

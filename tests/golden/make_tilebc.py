@@ -4,7 +4,7 @@ from the reference's own cuTile kernels.
 Run in a container where the reference tree is mounted (it is read, never
 written) and the cuda.tile package is installed (1.3.0 was used):
 
-    python tests/golden/make_tilebc.py /root/reference
+    python tests/golden/make_tilebc.py <path of the reference tree>
 
 Every module is produced here, from source, by cuda.tile's bytecode export:
 
