@@ -460,27 +460,58 @@ def host_link_probe(dev, h2d_bytes, d2h_bytes, dist_on):
     s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
 
     def timed(do_in, do_out, reps=3):
-        best = float("inf")
+        """Best of `reps`: (wall s, H2D s, D2H s), the per-direction times from
+        events on each copy stream, all started together."""
+        best = (float("inf"), 0.0, 0.0)
         for _ in range(reps):
             torch.cuda.synchronize(dev)
             if dist_on:
                 import torch.distributed as dist
                 dist.barrier()
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
             t0 = time.perf_counter()
             if do_in:
                 with torch.cuda.stream(s_in):
+                    ev[0].record()
                     d_in.copy_(h_in, non_blocking=True)
+                    ev[1].record()
             if do_out:
                 with torch.cuda.stream(s_out):
+                    ev[2].record()
                     h_out.copy_(d_out, non_blocking=True)
+                    ev[3].record()
             torch.cuda.synchronize(dev)
-            best = min(best, time.perf_counter() - t0)
+            wall = time.perf_counter() - t0
+            if wall < best[0]:
+                best = (wall, ev[0].elapsed_time(ev[1]) / 1e3 if do_in else 0.0,
+                        ev[2].elapsed_time(ev[3]) / 1e3 if do_out else 0.0)
         return best
-    t_in, t_out, t_both = timed(True, False), timed(False, True), timed(True, True)
+    t_in, t_out, (t_both, t_in_c, t_out_c) = timed(True, False)[0], timed(False, True)[0], timed(True, True)
     bound_s = t_both if h2d_bytes and d2h_bytes else max(t_in * h2d_bytes / nb_in, t_out * d2h_bytes / nb_out)
     return {"h2d_GBps": round(nb_in / t_in / 1e9, 1), "d2h_GBps": round(nb_out / t_out / 1e9, 1),
-            "both_GBps": round((nb_in + nb_out) / t_both / 1e9, 1), "ms_per_step": round(bound_s * 1e3, 3),
+            "both_GBps": round((nb_in + nb_out) / t_both / 1e9, 1),
+            "h2d_GBps_concurrent": round(nb_in / max(t_in_c, 1e-9) / 1e9, 1),
+            "d2h_GBps_concurrent": round(nb_out / max(t_out_c, 1e-9) / 1e9, 1),
+            "ms_per_step": round(bound_s * 1e3, 3),
             "how": "pinned copies of this step's H2D and D2H byte counts on two streams at once (best of 3)"}
+
+
+def growing_blocks_bound_ms(h2d_bytes, d2h_bytes, h2d_gbps, d2h_gbps):
+    """Least time of a pipelined C = A @ B over the host link whose output can
+    leave only after its inputs arrived.  Row blocks of A and column blocks of
+    B arrive together, so after a fraction f of the input bytes a fraction f^2
+    of C is computable (the most any order gives for that much input).  With
+    the input done at T_in = in / r_in, the output's copy-out is limited by
+    what is available until t* = r_out T_in^2 / (2 out), and by r_out after
+    that: T = t* + out (1 - (t* / T_in)^2) / r_out (T = T_in when t* >= T_in)."""
+    r_in, r_out = h2d_gbps * 1e9, d2h_gbps * 1e9
+    t_in = h2d_bytes / r_in
+    if d2h_bytes <= 0:
+        return t_in * 1e3
+    t_star = r_out * t_in * t_in / (2.0 * d2h_bytes)
+    if t_star >= t_in:
+        return t_in * 1e3
+    return (t_star + d2h_bytes * (1.0 - (t_star / t_in) ** 2) / r_out) * 1e3
 
 
 def e2e_matmul(wl, args, a, b, bias, out_dt, rows, dist_on):
@@ -525,10 +556,20 @@ def e2e_matmul(wl, args, a, b, bias, out_dt, rows, dist_on):
     # per rank: its rows of A and its 1/N of B's rows in, its rows of C out
     world = torch.distributed.get_world_size() if dist_on else 1
     rank_h2d = ha.numel() * ha.element_size() + hb.numel() * hb.element_size() // world
-    link = host_link_probe(a.device, rank_h2d, hc.numel() * hc.element_size(), dist_on)
+    rank_d2h = hc.numel() * hc.element_size()
+    link = host_link_probe(a.device, rank_h2d, rank_d2h, dist_on)
     bound_ms = max_over_ranks(link["ms_per_step"], dist_on)
     link["value"] = round(total_flops / (bound_ms / 1e3) / 1e12, 3)
     link["frac"] = round(value / link["value"], 4)
+    # the same link with the dependency of C on A's rows and B's columns
+    sched_ms = max_over_ranks(growing_blocks_bound_ms(rank_h2d, rank_d2h, link["h2d_GBps_concurrent"],
+                                                      link["d2h_GBps_concurrent"]), dist_on)
+    link["schedule_ms_per_step"] = round(sched_ms, 3)
+    link["schedule_value"] = round(total_flops / (sched_ms / 1e3) / 1e12, 3)
+    link["schedule_frac"] = round(value / link["schedule_value"], 4)
+    link["schedule_how"] = ("C's blocks leave only after their rows of A and columns of B arrived: with rows "
+                            "and columns growing together, f of the input makes f^2 of C; time = input at the "
+                            "concurrent H2D rate, output at the concurrent D2H rate under that availability")
     return {"value": round(value, 3), "unit": "TFLOP/s", "h2d_bytes_per_step": int(h2d),
             "d2h_bytes_per_step": int(d2h), "steps": steps, "how": how + " per step, host wall clock",
             "link_bound": link}
