@@ -68,6 +68,9 @@ def parse_args():
                         "all-gather of the row blocks")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-sweep", action="store_true", help="vector_add_1d: skip the N = 2^20 .. 2^28 sweep")
+    p.add_argument("--m", type=int, default=None,
+                   help="matmul: rows of C in place of the configuration's M (a single GPU's share of a sharded "
+                        "run, e.g. 1024 = 8192 / 8, for profiling)")
     p.add_argument("--sustain-steps", type=int, default=300,
                    help="matmul: after the timed steps, this many more back to back, reported under "
                         "'sustained' with their own clock record (0: skip)")
@@ -890,7 +893,9 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
                                 device_id=torch.device("cuda", local))
     peaks = measured_peaks()
-    wl = WORKLOADS[args.workload]
+    wl = dict(WORKLOADS[args.workload])
+    if args.m is not None and wl["kind"] == "matmul":
+        wl["m"] = args.m
     try:
         if wl["kind"] == "matmul":
             res = run_matmul(wl, args, rank, world, local, dist_on, peaks)
