@@ -1056,7 +1056,7 @@ __global__ void __cluster_dims__(2, 1, 1)
                     break;
                 }
                 const uint8_t *raw = raw_of(r);
-                uint8_t *st_ = smem + s * Cfg::kStageBytes;
+                uint8_t *stage = smem + s * Cfg::kStageBytes;
                 // A: the same swizzled layout in and out, 16-byte chunk by chunk
 #pragma unroll
                 for (int q = 0; q < X3PairCfg::kABytes / 16 / (32 * kX3ConvWarps); ++q) {
@@ -1064,11 +1064,11 @@ __global__ void __cluster_dims__(2, 1, 1)
                     const float4 x = reinterpret_cast<const float4 *>(raw)[c];
                     float4 hi, lo;
                     split4(x, hi, lo);
-                    reinterpret_cast<float4 *>(st_)[c] = hi;
-                    reinterpret_cast<float4 *>(st_ + X3PairCfg::kABytes)[c] = lo;
+                    reinterpret_cast<float4 *>(stage)[c] = hi;
+                    reinterpret_cast<float4 *>(stage + X3PairCfg::kABytes)[c] = lo;
                 }
                 const uint8_t *rawb = raw + X3PairCfg::kABytes;
-                uint8_t *bhi = st_ + 2 * X3PairCfg::kABytes, *blo = bhi + X3PairCfg::kBBytes;
+                uint8_t *bhi = stage + 2 * X3PairCfg::kABytes, *blo = bhi + X3PairCfg::kBBytes;
                 if constexpr (B_MN) {
                     // raw box j holds columns [32 j, 32 j + 32) x 32 K rows, N contiguous:
                     // element (n = 32 j + t, k) at k * 128 + ((t / 4) ^ (k % 8)) * 16 + (t % 4) * 4,
