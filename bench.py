@@ -224,7 +224,7 @@ def matmul_buffer_sets(wl, rows):
     set_bytes = (rows * wl["k"] + wl["k"] * wl["n"]) * elem[wl["dtype"]] + rows * wl["n"] * elem[wl["out"]]
     if rows == 0 or set_bytes > L2_BYTES:
         return 1
-    return min(64, math.ceil(2 * L2_BYTES / set_bytes))
+    return min(64, 2 * L2_BYTES // set_bytes + 1)  # strictly more than twice the L2
 
 
 def flops_of(wl, rows):
@@ -588,7 +588,7 @@ def vector_add_sweep(dev, peaks, exps=(20, 22, 24, 26, 28)):
     rows = []
     for e in exps:
         n = 2 ** e
-        sets = min(64, max(1, math.ceil(2 * L2_BYTES / (12 * n))))
+        sets = min(64, max(1, 2 * L2_BYTES // (12 * n) + 1))
         bufs = [(torch.rand(n, device=dev) * 2 - 1, torch.rand(n, device=dev) * 2 - 1, torch.empty(n, device=dev))
                 for _ in range(sets)]
         steps = int(min(2000, max(20, 0.05 / (12 * n / (peaks["hbm_gbs"] * 1e9)))))
@@ -616,7 +616,7 @@ def run_vector_add(wl, args, rank, world, local, dist_on, peaks):
     n = e1 - e0
     bytes_per_step = 12 * n
     # enough buffer sets that one round trip exceeds twice the L2
-    sets = max(1, math.ceil(2 * L2_BYTES / max(1, bytes_per_step)))
+    sets = max(1, 2 * L2_BYTES // max(1, bytes_per_step) + 1)
     sets = min(sets, 64)
     g = torch.Generator(device=dev).manual_seed(wl["seed"] * 1000 + rank)
     shape_local = (n,) if len(wl["shape"]) == 1 else None
