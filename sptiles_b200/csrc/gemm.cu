@@ -537,11 +537,12 @@ constexpr int kPairHalfN = 128;  // columns of B each CTA stages
 #define ST_PAIR_STAGES 6
 #endif
 #ifndef ST_L2_POLICY
-// operand loads: 0 evict_normal, 1 evict_last, 2 A evict_last and B evict_first
+// operand loads: 0 evict_normal, 1 evict_last, 2 A evict_last and B evict_first,
+// 3 A evict_last and B evict_normal
 #define ST_L2_POLICY 1
 #endif
 
-#if ST_L2_POLICY == 0
+#if ST_L2_POLICY == 0 || ST_L2_POLICY == 3
 __device__ __forceinline__ uint64_t l2_policy_evict_normal() {
     uint64_t p;
     asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(p));
@@ -558,7 +559,7 @@ __device__ __forceinline__ uint64_t operand_l2_policy_a() {
 }
 
 __device__ __forceinline__ uint64_t operand_l2_policy_b() {
-#if ST_L2_POLICY == 0
+#if ST_L2_POLICY == 0 || ST_L2_POLICY == 3
     return l2_policy_evict_normal();
 #elif ST_L2_POLICY == 2
     return l2_policy_evict_first();
