@@ -242,9 +242,11 @@ def time_steps(fn, steps, warmup, stream, dist_on, graph=True, stats=None):
     the timed region is one replay of it: every step is still one full call
     of the hot path, but the host's per-call launch overhead leaves the
     timed region (what a launch-bound inner loop does in production).
-    Without it, an event between steps also gives each step's own device
-    time, summarised into ``stats`` when given (first / last / min / median /
-    max ms), which shows the clock settling under the power cap.
+    Without it and with ``stats``, the same steps run once more right after
+    the timed region with an event between steps (events between launches
+    would perturb the timed region itself), and each step's own device time
+    is summarised into ``stats`` (first / last / min / median / max ms),
+    which shows the clock settling under the power cap.
     Returns (ms, launches issued by the library for the timed steps).
     """
     import torch
@@ -269,10 +271,8 @@ def time_steps(fn, steps, warmup, stream, dist_on, graph=True, stats=None):
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
     stream = torch.cuda.current_stream()
-    marks = []
     if g is None:
         before = st.kernel_launches()
-        marks = [torch.cuda.Event(enable_timing=True) for _ in range(steps - 1)]
         # Keep the GPU busy (a spin of ~1 ms, before the start event) while the
         # host enqueues the first steps, so the timed region does not include
         # the GPU idling for the host's first launch: the steps still run back
@@ -284,17 +284,23 @@ def time_steps(fn, steps, warmup, stream, dist_on, graph=True, stats=None):
     else:
         for i in range(steps):
             fn(i)
-            if i < steps - 1:
-                marks[i].record(stream)
     end.record(stream)
     torch.cuda.synchronize()
     if g is None:
         launches = st.kernel_launches() - before
         if stats is not None and steps > 1:
-            ev = [start, *marks, end]
+            # the per-step pass (untimed as a whole)
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
+            torch.cuda._sleep(2_000_000)
+            ev[0].record(stream)
+            for i in range(steps):
+                fn(i)
+                ev[i + 1].record(stream)
+            torch.cuda.synchronize()
             per = [ev[i].elapsed_time(ev[i + 1]) for i in range(steps)]
             stats.update({"first": round(per[0], 5), "last": round(per[-1], 5), "min": round(min(per), 5),
-                          "median": round(statistics.median(per), 5), "max": round(max(per), 5)})
+                          "median": round(statistics.median(per), 5), "max": round(max(per), 5),
+                          "how": "the same steps again after the timed region, an event between steps"})
     if dist_on:
         dist.barrier()
     del g
