@@ -21,7 +21,10 @@ namespace st {
 namespace {
 
 constexpr int kThreads = 256;
-constexpr int kUnroll = 4;        // 16-byte vectors per thread per iteration
+#ifndef ST_VADD_UNROLL
+#define ST_VADD_UNROLL 2
+#endif
+constexpr int kUnroll = ST_VADD_UNROLL;  // 16-byte vectors per thread per iteration
 constexpr int kCtasPerSm = 8;     // 2048 resident threads per SM
 
 __device__ __forceinline__ float4 load_stream(const float4 *p) {
