@@ -235,6 +235,17 @@ def flops_of(wl, rows):
 
 
 # ------------------------------------------------------------------ our arm
+def gpu_spin(stream, cycles=2_000_000):
+    """A ~1 ms busy kernel on `stream` (torch's spin kernel), so that the host
+    can queue the next launches before the GPU reaches them; skipped where
+    this torch has no such kernel."""
+    import torch
+    spin = getattr(torch.cuda, "_sleep", None)
+    if spin is not None:
+        with torch.cuda.stream(stream):
+            spin(cycles)
+
+
 def time_steps(fn, steps, warmup, stream, dist_on, graph=True, stats=None):
     """Device time (ms) of `steps` calls of `fn` after `warmup` calls.
 
@@ -277,7 +288,7 @@ def time_steps(fn, steps, warmup, stream, dist_on, graph=True, stats=None):
         # host enqueues the first steps, so the timed region does not include
         # the GPU idling for the host's first launch: the steps still run back
         # to back as the host issues them, and the events bracket exactly them.
-        torch.cuda._sleep(2_000_000)
+        gpu_spin(stream)
     start.record(stream)
     if g is not None:
         g.replay()
@@ -291,7 +302,7 @@ def time_steps(fn, steps, warmup, stream, dist_on, graph=True, stats=None):
         if stats is not None and steps > 1:
             # the per-step pass (untimed as a whole)
             ev = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
-            torch.cuda._sleep(2_000_000)
+            gpu_spin(stream)
             ev[0].record(stream)
             for i in range(steps):
                 fn(i)
